@@ -1,0 +1,376 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 BF16 attention forward (one JSON line on stdout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Workload: B=32, H=8, Sq=Sk=4096, D=128, BSHD
+contiguous, Q/K/V BF16 N(0,1) (torch RNG, seed 1 + rank), scale 1/sqrt(128),
+LSE off, O buffers reused. One step = one dense and one top-left causal
+forward through the C ABI (fav4_bshd_forward), i.e. the reference's two
+headline cases. FLOPs use the reference's convention (benchmarks/bshd.py:168-
+170): dense 4*B*H*D*S^2, causal 4*B*H*D*S(S+1)/2.
+
+Multi-GPU: one process per GPU; each rank runs the same per-GPU workload on
+its own shard of a global batch of 32*N (batch sharding needs no collective),
+so scaling is weak. Timing: W warm-up steps, then exactly K steps between a
+barrier + synchronize on both sides, CUDA events on the launching stream, max
+over ranks. Inputs (1 GiB per GPU) exceed the 126 MB L2, so no flush is needed.
+
+`value` is aggregate TFLOP/s over all ranks with inputs resident in HBM.
+`e2e` is the same metric with Q/K/V copied from pinned host memory and both
+outputs copied back inside the timed region. `roofline` relates the dense
+kernel's launches (timed with events around each launch) to the measured
+dense-BF16 peak. `cpu_baseline` (rank 0, N=1) times the FP64 CPU oracle --
+the reference's benchmarks/bshd.py:90-100 math -- on a bounded sample.
+
+--impl reference times that same CPU oracle as the reference arm: the
+reference implementation is HIP for AMD gfx1250 and cannot run here, so the
+reference's own CPU math (numpy FP64 port) is what is timed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "flash-attention-v4-rocm_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+B, H, S, D = 32, 8, 4096, 128
+METRIC = "fwd TFLOPS (B32 H8 D128 S4096, dense+causal step; aggregate over GPUs)"
+UNIT = "TFLOP/s"
+
+
+def flops(b, h, s, causal):
+    area = s * (s + 1) // 2 if causal else s * s
+    return 4 * b * h * D * area
+
+
+STEP_FLOPS = flops(B, H, S, False) + flops(B, H, S, True)
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per dense launch from the committed ncu summary, if any."""
+    try:
+        return json.loads((ROOT / "profiles" / "traffic.json").read_text())
+    except (OSError, ValueError):
+        return None
+
+
+# ------------------------------------------------------------ clocks ----
+class ClockSampler:
+    """Polls NVML (read-only) for SM clock and throttle reasons."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000001: "gpu_idle",
+    }
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], set()
+        self._stop = threading.Event()
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001 - NVML is optional telemetry
+            self.error = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.thread.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------- CPU baseline ----
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:  # noqa: BLE001
+        return 1
+
+
+def cpu_sample(budget_s: float, seed: int = 1, rows_per_slice: int | None = None):
+    """Time the FP64 CPU oracle on (batch, head) slices of the workload, dense
+    and causal alternately, until `budget_s` elapses (at least one of each).
+    Returns (TFLOP/s, description)."""
+    import numpy as np
+
+    from oracle import ref_attention as R
+    rng = np.random.default_rng(seed)
+    q = R.bf16_round(rng.standard_normal((1, S, 1, D), dtype=np.float32))
+    k = R.bf16_round(rng.standard_normal((1, S, 1, D), dtype=np.float32))
+    v = R.bf16_round(rng.standard_normal((1, S, 1, D), dtype=np.float32))
+    if rows_per_slice is None or rows_per_slice >= S:
+        rows = np.arange(S)
+    else:
+        rows = np.linspace(0, S - 1, rows_per_slice).astype(np.int64)
+    f_dense = 4 * D * len(rows) * S
+    f_causal = 4 * D * int((rows + 1).sum())
+    done = {False: 0, True: 0}
+    t0 = time.perf_counter()
+    spent = 0.0
+    total_flops = 0
+    while spent < budget_s or not (done[False] and done[True]):
+        causal = done[False] > done[True]
+        R.reference(q, k, v, causal, rows)
+        done[causal] += 1
+        total_flops += f_causal if causal else f_dense
+        spent = time.perf_counter() - t0
+    desc = (f"FP64 numpy oracle (benchmarks/bshd.py:90-100 math) on {done[False]} dense + {done[True]} causal "
+            f"(b,h) slices of B32 H8 S4096 ({len(rows)} of {S} query rows each), {spent:.1f} s")
+    return total_flops / spent / 1e12, desc
+
+
+# ------------------------------------------------------------ helpers ----
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+def run_reference_arm(args, rank, world):
+    """The reference arm: the CPU oracle, rank 0 only."""
+    if rank != 0:
+        return
+    # size each step so (W + K) steps take about two minutes in total
+    per_step = max(0.2, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    rows = S
+    # calibrate: one dense + one causal slice of 256 query rows
+    tf, _ = cpu_sample(0.0, rows_per_slice=256)
+    est_slice_s = 2 * flops(1, 1, S, False) / (tf * 1e12) * 0.75  # dense + causal
+    if est_slice_s > per_step:
+        rows = max(64, int(S * per_step / est_slice_s))
+    for _ in range(args.warmup):
+        cpu_sample(0.0, rows_per_slice=rows)
+    vals, descs = [], []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, d = cpu_sample(0.0, rows_per_slice=rows)
+        vals.append(v)
+        descs.append(d)
+    wall = time.perf_counter() - t0
+    value = statistics.mean(vals)
+    cores = cpu_threads()
+    sample = (f"per step: one dense + one causal (b,h) slice of B32 H8 S4096 with {rows} of {S} query rows, "
+              f"FP64 numpy oracle of benchmarks/bshd.py:90-100; the reference's kernel is HIP for gfx1250")
+    emit({"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+          "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+          "config": {"workload": "B32 H8 Sq=Sk=4096 D128 BSHD dense+causal (BASELINE configs[1]); CPU sample",
+                     "batch_per_gpu": B, "heads": H, "seq_len": S, "head_dim": D, "lse": False},
+          "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=0, help="fav4 config id (0 = Auto)")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle timing (N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import fav4_bshd
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    lib = fav4_bshd.load_library()
+    runner = fav4_bshd.Runner(lib)
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    q, k, v = (torch.randn((B, S, H, D), generator=gen, device=dev, dtype=torch.bfloat16) for _ in range(3))
+    o_dense, o_causal = torch.empty_like(q), torch.empty_like(q)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        runner.call(q, k, v, o_dense, None, False, args.config)
+        if ev is not None:
+            ev[1].record(stream)
+        runner.call(q, k, v, o_causal, None, True, args.config)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        nvml_index = torch.cuda._get_nvml_device_index(dev)
+    except Exception:  # noqa: BLE001
+        nvml_index = local
+    sampler = ClockSampler(nvml_index)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    dense_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    causal_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * STEP_FLOPS * args.steps / (ms_max * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with host buffers ----
+    e2e_steps = max(3, min(10, args.steps // 10))
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    ho_d = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    ho_c = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        runner.call(dq, dk, dv, o_dense, None, False, args.config)
+        runner.call(dq, dk, dv, o_causal, None, True, args.config)
+        ho_d.copy_(o_dense, non_blocking=True)
+        ho_c.copy_(o_causal, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * STEP_FLOPS * e2e_steps / (float(te.item()) * 1e-3) / 1e12
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = 2 * q.numel() * q.element_size()
+    ok_e2e = torch.equal(ho_d, o_dense.cpu()) and torch.equal(ho_c, o_causal.cpu())
+
+    status = runner.pipeline_status(clear=False)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    pk, pk_kind = peaks()
+    dense_avg = statistics.mean(dense_ms)
+    achieved = flops(B, H, S, False) / (dense_avg * 1e-3) / 1e12
+    long_region = ms_max > 2000.0
+    peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
+    traffic = committed_traffic()
+    roofline = {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel (dense, config Auto=2)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16",
+                "traffic": traffic.get("dense_dram_bytes_per_launch") if traffic else None,
+                "algorithmic_flops_per_launch": flops(B, H, S, False),
+                "algorithmic_bytes_per_launch": 4 * B * S * H * D * 2,
+                "dense_ms_median": statistics.median(dense_ms), "causal_ms_median": statistics.median(causal_ms),
+                "dense_tflops": achieved,
+                "causal_tflops": flops(B, H, S, True) / (statistics.mean(causal_ms) * 1e-3) / 1e12,
+                "frac_of_nominal_2250": achieved / 2250.0}
+    out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "B32 H8 Sq=Sk=4096 D128 BSHD, one dense + one causal forward per step "
+                                  "(BASELINE configs[1])",
+                      "batch_per_gpu": B, "global_batch": B * world, "heads": H, "seq_len": S, "head_dim": D,
+                      "lse": False, "fav4_config": args.config,
+                      "parallelism": f"batch-sharded x{world}, no collective",
+                      "l2": "inputs 1 GiB per GPU > 126 MB L2 (no flush)"},
+           "gpu_launches": 2 * args.steps,
+           "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                   "steps": e2e_steps, "outputs_match": ok_e2e},
+           "roofline": roofline, "clocks": sampler.summary(), "pipeline_status": status}
+    if world == 1 and not args.no_cpu_baseline:
+        v_cpu, desc = cpu_sample(args.cpu_budget)
+        out["cpu_baseline"] = {"value": v_cpu, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                               "sample": desc}
+    emit(out)
+
+
+if __name__ == "__main__":
+    main()

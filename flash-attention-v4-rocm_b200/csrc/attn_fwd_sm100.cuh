@@ -1,0 +1,478 @@
+// BF16 attention forward for B200 (sm_100a), native BSHD layout, head dim 128.
+//
+// Replaces the reference's single fused kernel `bshd_kernel`
+// (src/bshd_kernel.hpp:50-211) with a warp-specialised tcgen05 pipeline:
+//
+//   warp 8  (load)     TMA: Q tiles once per work tile, then a K/V ring
+//                      (K0,V0,K1,V1,...) through STAGES 32 KiB slots.
+//   warp 9  (mma)      one thread issues tcgen05.mma: S_i = Q_i K^T into TMEM,
+//                      O_i += P_i V with P_i read back from TMEM.
+//   warps 0-3 / 4-7    softmax for Q tile 0 / Q tile 1: one TMEM lane (= one
+//                      query row) per thread; exp2 online softmax with the lazy
+//                      rescale of bshd_kernel.hpp:155-164 (threshold 8 base-2
+//                      units); the rare O correction is done in TMEM by the row
+//                      owner; epilogue O/l -> BF16 and LSE (bshd_kernel.hpp:195-210).
+//
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// P_i (BF16 pairs, 64 columns) overwrites the first half of S_i.
+//
+// A CTA is persistent and walks work tiles (batch, head, block of QTILES*128
+// query rows) with a static stride of gridDim.x. Causal work tiles are ordered
+// batch by batch, heads interleaved, longest first (the order of
+// bshd_kernel.hpp:56-59); dense work tiles keep the query blocks of one head
+// adjacent so the K/V stream of that head is shared through L2.
+#pragma once
+#include <cuda_bf16.h>
+#include <cstdint>
+#include "sm100.cuh"
+
+namespace fav4 {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;  // query rows per Q tile (= TMEM lanes)
+constexpr int kBlockN = 128;  // keys per K/V tile
+constexpr int kBoxBytes = 128 * 64 * 2;          // one TMA box: 128 rows x 64 bf16
+constexpr int kTileBytes = 2 * kBoxBytes;        // a 128 x 128 bf16 tile = 32 KiB
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;        // base-2 units, bshd_kernel.hpp:157
+
+struct FwdParams {
+  __nv_bfloat16* o;
+  float* lse;
+  int batch, heads, sq, sk;
+  int kv_begin, kv_end;  // keys [kv_begin, kv_end) are attended (split-KV slices)
+  float scale_log2;      // scale * log2(e)
+  int num_mblocks;       // query blocks of QTILES*128 rows per (batch, head)
+  int num_tiles;         // batch * heads * num_mblocks
+  uint32_t* status;
+  uint64_t wait_limit_ns;
+};
+
+struct TileCoord {
+  int b, h, m0;  // m0 = first query row of the work tile
+};
+
+template <bool Causal, int QTiles>
+__device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
+  TileCoord c;
+  if (Causal) {
+    const int per_batch = p.heads * p.num_mblocks;
+    c.b = t / per_batch;
+    const int w = t - c.b * per_batch;
+    c.h = w % p.heads;
+    c.m0 = (p.num_mblocks - 1 - w / p.heads) * (QTiles * kBlockM);
+  } else {
+    const int bh = t / p.num_mblocks;
+    c.b = bh / p.heads;
+    c.h = bh - c.b * p.heads;
+    c.m0 = (t - bh * p.num_mblocks) * (QTiles * kBlockM);
+  }
+  return c;
+}
+
+// Number of K/V tiles Q tile `i` of a work tile needs (0 = tile skipped).
+template <bool Causal>
+__device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int r0) {
+  if (r0 >= p.sq) return 0;  // no real query row in this Q tile
+  int hi = p.kv_end;
+  if (Causal) hi = min(hi, r0 + kBlockM);  // top-left causal: key c visible to row r iff c <= r
+  if (hi <= p.kv_begin) return 0;
+  return (hi - p.kv_begin + kBlockN - 1) / kBlockN;
+}
+
+template <int Stages>
+struct SmemLayout {
+  static constexpr int kQ = 0;                               // QTILES x 32 KiB (always room for 2)
+  static constexpr int kKV = 2 * kTileBytes;                 // Stages x 32 KiB
+  static constexpr int kBar = kKV + Stages * kTileBytes;     // mbarriers
+  // barrier slots (8 bytes each)
+  static constexpr int kQFull = 0, kQEmpty = 1, kKVFull = 2, kKVEmpty = 2 + Stages;
+  static constexpr int kSFull = 2 + 2 * Stages, kPFull = kSFull + 2, kOFull = kPFull + 2, kOEmpty = kOFull + 2;
+  static constexpr int kNumBars = kOEmpty + 2 + 1;           // + teardown barrier
+  static constexpr int kTeardown = kNumBars - 1;
+  static constexpr int kTmemHolder = kBar + kNumBars * 8;
+  static constexpr int kAbort = kTmemHolder + 4;
+  static constexpr int kBytes = kAbort + 4;
+  static constexpr int kAlloc = kBytes + 1024;               // slack for 1 KiB alignment
+};
+
+// Ring position shared by the producer (load warp) and consumer (mma warp).
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  template <int Stages>
+  __device__ __forceinline__ void advance() {
+    if (++stage == Stages) { stage = 0; phase ^= 1u; }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// exp2 split between MUFU and an FMA polynomial.
+// The polynomial path: 2^x = 2^j * 2^f with j = round-to-nearest(x) taken from
+// the mantissa of x + 1.5*2^23, f = x - j in [-0.5, 0.5], and
+// 2^f ~ 1 + c1 f + c2 f^2 + c3 f^3, a minimax fit of the relative error with
+// the constant term pinned to 1 (so x = 0, the row maximum, is exact; max
+// relative error 1.01e-4), computed for this library by a linear program
+// (fav4_bshd/exp2_poly.py). 2^j is added into the exponent field with an
+// integer add. x is clamped at -126 so the exponent never borrows into the
+// sign bit, and anything below -126 (masked keys are -inf) returns exactly 0.
+// ---------------------------------------------------------------------------
+constexpr float kPolyC1 = 0.6932829022407532f;
+constexpr float kPolyC2 = 0.2422109693288803f;
+constexpr float kPolyC3 = 0.055009059607982635f;
+
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float t = fmaxf(x, -126.0f);
+  const float r = __fadd_rn(t, 12582912.0f);  // 1.5 * 2^23: integer part lands in the low mantissa bits
+  const float j = __fsub_rn(r, 12582912.0f);
+  const float f = __fsub_rn(t, j);
+  float q = __fmaf_rn(kPolyC3, f, kPolyC2);
+  q = __fmaf_rn(q, f, kPolyC1);
+  q = __fmaf_rn(q, f, 1.0f);
+  const float y = __uint_as_float(__float_as_uint(q) + (__float_as_uint(r) << 23));
+  return x < -126.0f ? 0.0f : y;
+}
+
+// Columns c with (c % 8) < PolyPer8 use the polynomial, the rest MUFU ex2.
+template <int PolyPer8>
+__device__ __forceinline__ float ex2_split(float x, int c) {
+  if (PolyPer8 > 0 && (c % 8) < PolyPer8) return ex2_poly(x);
+  return ex2_mufu(x);
+}
+
+// ---------------------------------------------------------------------------
+template <bool Causal, int QTiles, int Stages, int PolyPer8>
+__global__ void __launch_bounds__(384, 1)
+    attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using L = SmemLayout<Stages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + L::kBar;
+  auto bar = [&](int slot) -> uint32_t { return bar0 + 8u * slot; };
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kAbort);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kTmemHolder);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  WaitCtl ctl{abort_flag, p.status, p.wait_limit_ns};
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0u;
+    mbar_init(bar(L::kQFull), 1);
+    mbar_init(bar(L::kQEmpty), 1);
+    for (int s = 0; s < Stages; ++s) {
+      mbar_init(bar(L::kKVFull + s), 1);
+      mbar_init(bar(L::kKVEmpty + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(L::kSFull + i), 1);
+      mbar_init(bar(L::kPFull + i), 128);
+      mbar_init(bar(L::kOFull + i), 1);
+      mbar_init(bar(L::kOEmpty + i), 128);
+    }
+    mbar_init(bar(L::kTeardown), 1);
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_addr(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 8) {
+    // ============================ TMA producer ============================
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      const uint64_t pol_q = policy_evict_first();
+      Ring ring;
+      uint32_t q_empty_par = 1;
+      // parity each stage was last armed with, for the drain on abort
+      uint32_t armed_mask = 0, armed_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+        const int n0 = kv_tiles_for<Causal>(p, tc.m0);
+        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc.m0 + kBlockM) : 0;
+        const int N = max(n0, n1);
+        if (N == 0) continue;
+        if (!mbar_wait(bar(L::kQEmpty), q_empty_par, ctl, kStatusTimeoutLoad)) { ok = false; break; }
+        q_empty_par ^= 1u;
+        const int nq = (n0 > 0 ? 1 : 0) + (n1 > 0 ? 1 : 0);
+        mbar_arrive_expect_tx(bar(L::kQFull), nq * kTileBytes);
+        for (int i = 0; i < QTiles; ++i) {
+          if ((i == 0 ? n0 : n1) == 0) continue;
+          const uint32_t dst = sbase + L::kQ + i * kTileBytes;
+          tma_load_4d(dst, &tm_q, bar(L::kQFull), 0, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
+          tma_load_4d(dst + kBoxBytes, &tm_q, bar(L::kQFull), 64, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
+        }
+        for (int j = 0; j < N && ok; ++j) {
+          const int s0 = p.kv_begin + j * kBlockN;
+#pragma unroll 1
+          for (int which = 0; which < 2; ++which) {
+            if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = bar(L::kKVFull + ring.stage);
+            mbar_arrive_expect_tx(fb, kTileBytes);
+            armed_mask |= 1u << ring.stage;
+            armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
+            const uint32_t dst = sbase + L::kKV + ring.stage * kTileBytes;
+            const CUtensorMap* m = which == 0 ? &tm_k : &tm_v;
+            tma_load_4d(dst, m, fb, 0, tc.h, s0, tc.b, pol_kv);
+            tma_load_4d(dst + kBoxBytes, m, fb, 64, tc.h, s0, tc.b, pol_kv);
+            ring.advance<Stages>();
+          }
+        }
+      }
+      if (!ok) {
+        // Let every copy this warp issued land before the CTA exits.
+        WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
+        volatile uint32_t no_abort = 0;
+        drain.abort = &no_abort;
+        for (int s = 0; s < Stages; ++s)
+          if (armed_mask & (1u << s)) mbar_wait(bar(L::kKVFull + s), (armed_par >> s) & 1u, drain, kStatusTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ============================= MMA issuer =============================
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(kBlockM, kBlockN, false);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kBlockM, kHeadDim, true);
+      Ring ring;
+      uint32_t q_full_par = 0, p_par[2] = {0, 0}, o_empty_par[2] = {1, 1};
+      bool ok = true;
+      auto issue_s = [&](int i, int kstage) {
+        const uint32_t qa = sbase + L::kQ + i * kTileBytes;
+        const uint32_t ka = sbase + L::kKV + kstage * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k) {
+          const uint32_t off = (k / 4) * kBoxBytes + (k % 4) * 32;
+          umma_ss(tmem + i * 128, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(ka + off, 16, 1024),
+                  idesc_qk, k > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(L::kSFull + i));
+      };
+      auto issue_pv = [&](int i, int vstage, bool acc) {
+        const uint32_t va = sbase + L::kKV + vstage * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kBlockN / 16; ++k) {
+          umma_ts(tmem + 256 + i * 128, tmem + i * 128 + k * 8, make_sdesc_sw128(va + k * 2048, kBoxBytes, 1024),
+                  idesc_pv, (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+        const int n0 = kv_tiles_for<Causal>(p, tc.m0);
+        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc.m0 + kBlockM) : 0;
+        const int N = max(n0, n1);
+        if (N == 0) continue;
+        if (!mbar_wait(bar(L::kQFull), q_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
+        q_full_par ^= 1u;
+        // K(0)
+        int kstage = ring.stage;
+        if (!mbar_wait(bar(L::kKVFull + kstage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+        ring.advance<Stages>();
+        tc_fence_after();
+        if (n0 > 0) issue_s(0, kstage);
+        if (n1 > 0) issue_s(1, kstage);
+        tc_commit(bar(L::kKVEmpty + kstage));
+        if (N == 1) tc_commit(bar(L::kQEmpty));
+        for (int j = 0; j < N && ok; ++j) {
+          const int vstage = ring.stage;
+          if (!mbar_wait(bar(L::kKVFull + vstage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+          ring.advance<Stages>();
+          const bool next_k = j + 1 < N;
+          int nk_stage = -1;
+          uint32_t nk_phase = 0;
+          bool nk_ready = false;
+          if (next_k) {
+            nk_stage = ring.stage;
+            nk_phase = ring.phase;
+            ring.advance<Stages>();
+          }
+#pragma unroll 1
+          for (int i = 0; i < QTiles; ++i) {
+            const int ni = i == 0 ? n0 : n1;
+            if (j >= ni) continue;
+            if (!mbar_wait(bar(L::kPFull + i), p_par[i], ctl, kStatusTimeoutMma)) { ok = false; break; }
+            p_par[i] ^= 1u;
+            if (j == 0) {
+              if (!mbar_wait(bar(L::kOEmpty + i), o_empty_par[i], ctl, kStatusTimeoutMma)) { ok = false; break; }
+              o_empty_par[i] ^= 1u;
+            }
+            tc_fence_after();
+            issue_pv(i, vstage, j > 0);
+            if (j + 1 == ni) tc_commit(bar(L::kOFull + i));
+            if (j + 1 < ni) {
+              if (!nk_ready) {
+                if (!mbar_wait(bar(L::kKVFull + nk_stage), nk_phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+                nk_ready = true;
+                tc_fence_after();
+              }
+              issue_s(i, nk_stage);
+            }
+          }
+          if (!ok) break;
+          tc_commit(bar(L::kKVEmpty + vstage));
+          if (next_k) {
+            tc_commit(bar(L::kKVEmpty + nk_stage));
+            if (j + 2 == N) tc_commit(bar(L::kQEmpty));
+          }
+        }
+      }
+      // Every MMA this thread issued has finished once this barrier flips.
+      tc_commit(bar(L::kTeardown));
+      WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
+      volatile uint32_t no_abort = 0;
+      drain.abort = &no_abort;
+      mbar_wait(bar(L::kTeardown), 0, drain, kStatusTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp < 4 * QTiles) {
+    // ============================== softmax ===============================
+    const int i = warp / 4;                  // Q tile served by this warpgroup
+    const int row = (warp % 4) * 32 + lane;  // TMEM lane = row within the Q tile
+    const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + i * 128;
+    const uint32_t t_o = tmem + lane_off + 256 + i * 128;
+    uint32_t s_par = 0, o_full_par = 0;
+    const float scale_log2 = p.scale_log2;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+      const int r0 = tc.m0 + i * kBlockM;
+      const int ni = kv_tiles_for<Causal>(p, r0);
+      const int grow = r0 + row;  // query row (global within the sequence)
+      float m = -INFINITY, l = 0.f;
+      if (ni == 0) {
+        if (r0 >= p.sq) continue;  // padding-only Q tile: nothing to write
+      }
+      for (int j = 0; j < ni; ++j) {
+        if (!warp_wait(bar(L::kSFull + i), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+        s_par ^= 1u;
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sr[c]);
+        tmem_ld_wait();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c / 32][c % 32]);
+        const int col0 = p.kv_begin + j * kBlockN;
+        // Mask keys past kv_end, and (causal) keys after this row.
+        const bool tail = col0 + kBlockN > p.kv_end;
+        const bool diag = Causal && (col0 + kBlockN - 1 > r0);
+        if (tail || diag) {
+          int lim = p.kv_end - 1 - col0;  // last visible column index within the tile
+          if (Causal) lim = min(lim, grow - col0);
+#pragma unroll
+          for (int c = 0; c < 128; ++c) s[c] = c > lim ? -INFINITY : s[c];
+        }
+        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+#pragma unroll
+        for (int c = 4; c < 128; c += 4) {
+          mx0 = fmaxf(mx0, fmaxf(s[c], s[c + 1]));
+          mx1 = fmaxf(mx1, fmaxf(s[c + 2], s[c + 3]));
+        }
+        const float mx = fmaxf(mx0, mx1) * scale_log2;
+        const float cand = fmaxf(m, mx);
+        const bool update = (j == 0) || (cand > m + kRescaleThreshold);
+        const float m_new = update ? cand : m;
+        if (j > 0 && __any_sync(0xffffffffu, update)) {
+          // Lazy correction: O_i (which already holds P V of the previous
+          // tiles) is rescaled in TMEM by the row owner.
+          const float alpha = (m_new == -INFINITY) ? 1.f : ex2_mufu(m - m_new);
+          l *= alpha;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(t_o + c * 32, orow);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
+            tmem_st32(t_o + c * 32, orow);
+          }
+        }
+        m = m_new;
+        const float mb = (m == -INFINITY) ? 0.f : m;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[2][32];
+#pragma unroll
+        for (int c = 0; c < 128; c += 2) {
+          const float x0 = __fmaf_rn(s[c], scale_log2, -mb);
+          const float x1 = __fmaf_rn(s[c + 1], scale_log2, -mb);
+          const float e0 = ex2_split<PolyPer8>(x0, c);
+          const float e1 = ex2_split<PolyPer8>(x1, c + 1);
+          acc[(c / 2) % 4] += e0 + e1;
+          pk[c / 64][(c % 64) / 2] = pack_bf16x2(e0, e1);
+        }
+        l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        tmem_st32(t_s, pk[0]);
+        tmem_st32(t_s + 32, pk[1]);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(L::kPFull + i));
+      }
+      if (!ok) break;
+      // ------------------------------ epilogue ------------------------------
+      const bool live = grow < p.sq;
+      __nv_bfloat16* orow_ptr =
+          p.o + ((static_cast<int64_t>(tc.b) * p.sq + grow) * p.heads + tc.h) * kHeadDim;
+      if (ni > 0) {
+        if (!warp_wait(bar(L::kOFull + i), o_full_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+        o_full_par ^= 1u;
+        tc_fence_after();
+        const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t orow[32];
+          tmem_ld32(t_o + c * 32, orow);
+          tmem_ld_wait();
+          if (live) {
+            uint4* dst = reinterpret_cast<uint4*>(orow_ptr + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
+              dst[v] = w;
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(bar(L::kOEmpty + i));
+      } else if (live) {
+        uint4* dst = reinterpret_cast<uint4*>(orow_ptr);
+#pragma unroll
+        for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      if (live && p.lse != nullptr) {
+        p.lse[(static_cast<int64_t>(tc.b) * p.heads + tc.h) * p.sq + grow] =
+            l > 0.f ? m * kLn2 + logf(l) : -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fav4

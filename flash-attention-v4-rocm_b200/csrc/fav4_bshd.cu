@@ -1,0 +1,204 @@
+// Host side of the C ABI declared in include/fav4_bshd.h.
+//
+// fav4_bshd_forward keeps the reference's argument checks one for one
+// (src/bshd.hip:27-34), its Auto rule (src/bshd.hip:23-25) and its return
+// convention (invalid -> cudaErrorInvalidValue, else the launch status,
+// src/bshd.hip:17-19), then encodes TMA tensor maps for the BSHD tensors and
+// launches the persistent sm_100a kernel on the caller's stream. Nothing is
+// allocated and the host never synchronises.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "attn_fwd_sm100.cuh"
+#include "combine.cuh"
+#include "tensor_map.h"
+#include "fav4_bshd.h"
+
+namespace fav4 {
+
+__device__ uint32_t g_status;  // per-device pipeline status word (see fav4_bshd_pipeline_status)
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+uint64_t wait_limit_ns() {
+  static uint64_t limit = [] {
+    const char* env = std::getenv("FAV4_WAIT_LIMIT_MS");
+    long ms = env ? std::strtol(env, nullptr, 10) : 0;
+    if (ms <= 0) ms = 2000;
+    return static_cast<uint64_t>(ms) * 1000000ull;
+  }();
+  return limit;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  uint32_t* status = nullptr;
+};
+
+// Per-device facts fetched once: SM count and the device address of g_status.
+bool device_info(int dev, DeviceInfo* out) {
+  static std::mutex mu;
+  static DeviceInfo cache[kMaxDevices];
+  static bool ready[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ready[dev]) {
+    DeviceInfo d;
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_status) != cudaSuccess) return false;
+    d.status = static_cast<uint32_t*>(addr);
+    cache[dev] = d;
+    ready[dev] = true;
+  }
+  *out = cache[dev];
+  return true;
+}
+
+// The reference's argument checks (src/bshd.hip:27-34).
+bool args_valid(const Fav4Args* a, int causal, int config) {
+  if (!a || !a->q || !a->k || !a->v || !a->o || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->sk <= 0 ||
+      (causal != 0 && causal != 1) || config < 0 || config > 3 || !std::isfinite(a->scale) || a->scale <= 0)
+    return false;
+  if (a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128) ||
+      a->sk > INT_MAX / (a->heads * 128) ||
+      ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) | reinterpret_cast<uintptr_t>(a->v) |
+        reinterpret_cast<uintptr_t>(a->o)) &
+       15))
+    return false;
+  return true;
+}
+
+// B200 tilings behind the reference's config ids (include/fav4_bshd.h:17-18):
+//   1: one 128-row Q tile per CTA, 4-stage K/V ring, MUFU exp2 only
+//   2: two 128-row Q tiles per CTA sharing each K/V tile, 3-stage ring,
+//      1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
+//   3: two Q tiles, 4-stage ring, 1/2 of exp2 on the polynomial
+template <bool Causal, int QTiles, int Stages, int PolyPer8>
+int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  DeviceInfo info;
+  if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
+  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Stages, PolyPer8>;
+  constexpr int smem = SmemLayout<Stages>::kAlloc;
+  {
+    static std::mutex mu;
+    static bool attr_set[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  CUtensorMap tq, tk, tv;
+  if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, a.heads) ||
+      !encode_bshd(&tv, a.v, a.batch, a.sk, a.heads))
+    return cudaErrorInvalidValue;
+  FwdParams p;
+  p.o = static_cast<__nv_bfloat16*>(a.o);
+  p.lse = a.lse;
+  p.batch = a.batch;
+  p.heads = a.heads;
+  p.sq = a.sq;
+  p.sk = a.sk;
+  p.kv_begin = kv_begin;
+  p.kv_end = kv_end;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.num_mblocks = (a.sq + QTiles * kBlockM - 1) / (QTiles * kBlockM);
+  const int64_t tiles = static_cast<int64_t>(a.batch) * a.heads * p.num_mblocks;
+  if (tiles > INT_MAX) return cudaErrorInvalidValue;
+  p.num_tiles = static_cast<int>(tiles);
+  p.status = info.status;
+  p.wait_limit_ns = wait_limit_ns();
+  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError();
+}
+
+template <bool Causal>
+int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream) {
+  switch (config) {
+    case 1: return launch_fwd<Causal, 1, 4, 0>(a, kv_begin, kv_end, stream);
+    case 2: return launch_fwd<Causal, 2, 3, 2>(a, kv_begin, kv_end, stream);
+    case 3: return launch_fwd<Causal, 2, 4, 4>(a, kv_begin, kv_end, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_select_config(const Fav4Args* a) { return a->sq < 128 ? 1 : 2; }
+
+extern "C" int fav4_bshd_forward(const Fav4Args* a, int causal, int config, cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config)) return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream)
+                : fav4::dispatch<false>(*a, config, 0, a->sk, stream);
+}
+
+extern "C" int fav4_bshd_forward_partial(const Fav4Args* a, int causal, int config, int kv_begin, int kv_end,
+                                         cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || !a->lse || kv_begin < 0 || kv_end <= kv_begin || kv_end > a->sk ||
+      (reinterpret_cast<uintptr_t>(a->lse) & 3))
+    return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  return causal ? fav4::dispatch<true>(*a, config, kv_begin, kv_end, stream)
+                : fav4::dispatch<false>(*a, config, kv_begin, kv_end, stream);
+}
+
+extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts, int parts, void* o,
+                                 float* lse, int batch, int heads, int sq, cudaStream_t stream) {
+  if (!o_parts || !lse_parts || !o || parts < 1 || parts > fav4::kMaxCombineParts || batch <= 0 || heads <= 0 ||
+      sq <= 0 || batch > INT_MAX / heads || heads > INT_MAX / 128 || sq > INT_MAX / (heads * 128) ||
+      (reinterpret_cast<uintptr_t>(o) & 15))
+    return cudaErrorInvalidValue;
+  fav4::CombineParams p = {};
+  for (int g = 0; g < parts; ++g) {
+    if (!o_parts[g] || !lse_parts[g] || (reinterpret_cast<uintptr_t>(o_parts[g]) & 15) ||
+        (reinterpret_cast<uintptr_t>(lse_parts[g]) & 3))
+      return cudaErrorInvalidValue;
+    p.o[g] = static_cast<const __nv_bfloat16*>(o_parts[g]);
+    p.lse[g] = lse_parts[g];
+  }
+  p.parts = parts;
+  p.out = static_cast<__nv_bfloat16*>(o);
+  p.lse_out = lse;
+  p.batch = batch;
+  p.heads = heads;
+  p.sq = sq;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  fav4::DeviceInfo info;
+  if (!fav4::device_info(dev, &info)) return cudaErrorInvalidDevice;
+  const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
+  const int64_t want = (rows + 7) / 8;  // 8 warps per block, one row per warp per pass
+  const int64_t cap = static_cast<int64_t>(info.sms) * 8;
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  fav4::combine_kernel<<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+extern "C" int fav4_bshd_pipeline_status(int clear) {
+  uint32_t v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, fav4::g_status, sizeof(v)) != cudaSuccess) return -1;
+  if (clear) {
+    const uint32_t zero = 0;
+    if (cudaMemcpyToSymbol(fav4::g_status, &zero, sizeof(zero)) != cudaSuccess) return -1;
+  }
+  return static_cast<int>(v & 0x7fffffffu);
+}

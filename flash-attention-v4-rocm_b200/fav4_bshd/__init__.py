@@ -1,0 +1,162 @@
+"""Python host side of the B200 BF16 attention-forward library.
+
+Mirrors the reference's ctypes harness interface (benchmarks/bshd.py:18-20 for
+the ``Args`` structure, :56-74 for ``Runner.call``): the same struct layout,
+the same argument checks, the same error behaviour (a nonzero status raises
+RuntimeError). Everything runs through the C ABI in include/fav4_bshd.h,
+implemented by build/libfav4_bshd.so; there is no other code path, so a
+missing library is an error, never a fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from pathlib import Path
+
+PKG_ROOT = Path(__file__).resolve().parents[1]  # the flash-attention-v4-rocm_b200 folder
+BUILD_DIR = PKG_ROOT / "build"
+LIB_PATH = BUILD_DIR / "libfav4_bshd.so"
+PROBE_LIB_PATH = BUILD_DIR / "libfav4_probe.so"
+HEAD_DIM = 128
+CUDA_ERROR_INVALID_VALUE = 1
+
+
+class Args(C.Structure):
+    """Fav4Args (include/fav4_bshd.h), field for field as benchmarks/bshd.py:18-20."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "lse")] + [
+        (n, C.c_int) for n in ("batch", "heads", "sq", "sk")] + [("scale", C.c_float)]
+
+
+_LIB = None
+_PROBE = None
+
+
+def _bind(lib):
+    lib.fav4_bshd_forward.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_forward.restype = C.c_int
+    lib.fav4_bshd_select_config.argtypes = [C.POINTER(Args)]
+    lib.fav4_bshd_select_config.restype = C.c_int
+    lib.fav4_bshd_forward_partial.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_forward_partial.restype = C.c_int
+    lib.fav4_bshd_combine.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int, C.c_void_p,
+                                      C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_combine.restype = C.c_int
+    lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
+    lib.fav4_bshd_pipeline_status.restype = C.c_int
+    return lib
+
+
+def load_library(path: Path | str | None = None):
+    """Load (once) the CUDA library. Raises if it has not been built."""
+    global _LIB
+    if _LIB is None or path is not None:
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(f"{p} is missing: build it with `python -m fav4_bshd.build` "
+                               f"(or __graft_entry__.build()); there is no CPU fallback")
+        lib = _bind(C.CDLL(str(p)))
+        if path is not None:
+            return lib
+        _LIB = lib
+    return _LIB
+
+
+def load_probe_library():
+    """The test-only probe library (TMA / UMMA / bounded-wait probes)."""
+    global _PROBE
+    if _PROBE is None:
+        if not PROBE_LIB_PATH.exists():
+            raise RuntimeError(f"{PROBE_LIB_PATH} is missing: build it with `python -m fav4_bshd.build`")
+        lib = C.CDLL(str(PROBE_LIB_PATH))
+        lib.fav4_probe_tma_load.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        lib.fav4_probe_gemm_qk.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        lib.fav4_probe_gemm_pv.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        lib.fav4_probe_bounded_wait.argtypes = [C.c_int, C.c_void_p, C.c_void_p]
+        lib.fav4_probe_status.argtypes = [C.c_int]
+        for f in ("fav4_probe_tma_load", "fav4_probe_gemm_qk", "fav4_probe_gemm_pv", "fav4_probe_bounded_wait",
+                  "fav4_probe_status"):
+            getattr(lib, f).restype = C.c_int
+        _PROBE = lib
+    return _PROBE
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None):
+    import torch
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _check_bshd(q, k, v, o, lse):
+    import torch
+    assert all(x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous() for x in (q, k, v, o))
+    b, sq, h, d = q.shape
+    assert d == HEAD_DIM and k.shape == v.shape and k.shape[0] == b and k.shape[2:] == (h, d) and o.shape == q.shape
+    assert lse is None or (lse.shape == (b, h, sq) and lse.is_contiguous() and lse.dtype == torch.float32)
+    return b, sq, h
+
+
+class Runner:
+    """The reference harness's Runner (benchmarks/bshd.py:56-74), bound to this library."""
+
+    def __init__(self, lib=None):
+        self.lib = lib if lib is not None else load_library()
+
+    def args(self, q, k, v, o, lse, scale=None):
+        b, sq, h = _check_bshd(q, k, v, o, lse)
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        return Args(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, h, sq, k.shape[1], scale)
+
+    def call(self, q, k, v, o, lse, causal, config=0, scale=None, stream=None):
+        a = self.args(q, k, v, o, lse, scale)
+        status = self.lib.fav4_bshd_forward(C.byref(a), int(causal), config, _stream(stream))
+        if status:
+            raise RuntimeError(f"config {config}: CUDA status {status}")
+
+    def call_partial(self, q, k, v, o, lse, causal, kv_begin, kv_end, config=0, scale=None, stream=None):
+        a = self.args(q, k, v, o, lse, scale)
+        status = self.lib.fav4_bshd_forward_partial(C.byref(a), int(causal), config, kv_begin, kv_end,
+                                                    _stream(stream))
+        if status:
+            raise RuntimeError(f"partial [{kv_begin},{kv_end}) config {config}: CUDA status {status}")
+
+    def combine(self, o_parts, lse_parts, o, lse=None, stream=None):
+        import torch
+        n = len(o_parts)
+        assert n == len(lse_parts) and n >= 1
+        b, sq, h, d = o.shape
+        assert o.dtype == torch.bfloat16 and o.is_contiguous() and d == HEAD_DIM
+        for op, lp in zip(o_parts, lse_parts):
+            assert op.shape == o.shape and op.dtype == torch.bfloat16 and op.is_contiguous()
+            assert lp.shape == (b, h, sq) and lp.dtype == torch.float32 and lp.is_contiguous()
+        optrs = (C.c_void_p * n)(*[x.data_ptr() for x in o_parts])
+        lptrs = (C.c_void_p * n)(*[x.data_ptr() for x in lse_parts])
+        status = self.lib.fav4_bshd_combine(optrs, lptrs, n, o.data_ptr(), _ptr(lse), b, h, sq, _stream(stream))
+        if status:
+            raise RuntimeError(f"combine of {n} parts: CUDA status {status}")
+
+    def select_config(self, q, k, v, o, lse=None):
+        a = self.args(q, k, v, o, lse)
+        return self.lib.fav4_bshd_select_config(C.byref(a))
+
+    def pipeline_status(self, clear=True):
+        return self.lib.fav4_bshd_pipeline_status(1 if clear else 0)
+
+
+def forward(q, k, v, causal=False, config=0, scale=None, return_lse=False, out=None):
+    """Allocate O (and LSE) with torch and run fav4_bshd_forward on the current stream."""
+    import torch
+    o = torch.empty_like(q) if out is None else out
+    lse = torch.empty((q.shape[0], q.shape[2], q.shape[1]), device=q.device, dtype=torch.float32) \
+        if return_lse else None
+    Runner().call(q, k, v, o, lse, causal, config, scale)
+    return (o, lse) if return_lse else o
+
+
+__all__ = ["Args", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
+           "HEAD_DIM", "CUDA_ERROR_INVALID_VALUE"]

@@ -1,0 +1,79 @@
+/* C ABI of the B200 (sm_100a) BF16 attention-forward library.
+ *
+ * Drop-in for the reference's public header (include/fav4_bshd.h:1-20 of
+ * rocking5566/flash-attention-v4-rocm): same struct layout, same symbol names,
+ * same argument meaning and error codes, with cudaStream_t in place of
+ * hipStream_t (both are an opaque pointer, so ctypes callers are unchanged).
+ */
+#ifndef FAV4_BSHD_H_
+#define FAV4_BSHD_H_
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same field order and types as the reference's Fav4Args
+ * (include/fav4_bshd.h:4-10): 5 pointers, 4 ints, 1 float. */
+struct Fav4Args {
+  const void *q, *k, *v;
+  void* o;
+  float* lse;
+  int batch, heads, sq, sk;
+  float scale;
+};
+typedef struct Fav4Args Fav4Args;
+
+/* Contract (reference include/fav4_bshd.h:12-18):
+ * Q/K/V/O are contiguous BF16 [batch, sequence, heads, 128], device-resident,
+ * 16-byte aligned and non-overlapping. LSE is optional FP32 [batch, heads, sq]
+ * in natural-log units. Top-left causal (key c visible to query row r iff
+ * c <= r), equal Q/K/V heads, positive finite scale, finite dot products.
+ * The stream belongs to the calling device; the call allocates nothing and
+ * never synchronises the host, so it can be captured in a CUDA graph.
+ * config 0 = Auto (fav4_bshd_select_config), 1/2/3 = explicit tilings.
+ * Returns 0 on success, cudaErrorInvalidValue (1) on invalid arguments or
+ * config, else the launch status (cudaGetLastError).
+ *
+ * Replaces: fav4_bshd_forward, reference include/fav4_bshd.h:19 and
+ * src/bshd.hip:26-38. */
+int fav4_bshd_forward(const Fav4Args* args, int causal, int config, cudaStream_t stream);
+
+/* Auto configuration: 1 when sq < 128, else 2.
+ * Replaces: fav4_bshd_select_config, reference include/fav4_bshd.h:20 and
+ * src/bshd.hip:23-25. */
+int fav4_bshd_select_config(const Fav4Args* args);
+
+/* Split-KV slice (no reference counterpart; needed because Fav4Args carries
+ * no key offset). Attends only keys [kv_begin, kv_end) with absolute
+ * positions, so top-left causal masking stays correct for any slice. O is the
+ * slice-normalised output (BF16, zero for rows that see no key of the slice);
+ * LSE is required and is -inf for such rows. Same validation and return codes
+ * as fav4_bshd_forward, plus 0 <= kv_begin < kv_end <= sk. */
+int fav4_bshd_forward_partial(const Fav4Args* args, int causal, int config, int kv_begin, int kv_end,
+                              cudaStream_t stream);
+
+/* LSE-weighted combine of `parts` split-KV slices (no reference counterpart):
+ *   LSE = log(sum_g exp(LSE_g)),  O = sum_g exp(LSE_g - LSE) * O_g.
+ * o_parts[g] / lse_parts[g] are the outputs of fav4_bshd_forward_partial for
+ * the same (batch, heads, sq) and may live on peer GPUs with peer access
+ * enabled (read with plain loads). o and lse (lse may be NULL) receive the
+ * result; rows whose every slice is empty get O = 0 and LSE = -inf.
+ * 1 <= parts <= 16. Returns 0, cudaErrorInvalidValue or the launch status. */
+int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts, int parts, void* o, float* lse,
+                      int batch, int heads, int sq, cudaStream_t stream);
+
+/* Failure detection (no reference counterpart): every pipeline wait inside the
+ * kernels is bounded in time (default 2000 ms, environment variable
+ * FAV4_WAIT_LIMIT_MS). A wait that runs out makes the kernel stop cleanly and
+ * ORs a code into a per-device status word: 1 load, 2 mma, 4 softmax,
+ * 8 drain, 16 probe. This call synchronises the current device, returns the
+ * word (or -1 on a CUDA error) and clears it when `clear` is nonzero. */
+int fav4_bshd_pipeline_status(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAV4_BSHD_H_ */

@@ -1,0 +1,287 @@
+"""CPU oracle for the BF16 BSHD attention forward -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+arm may import this module, and only as the checker or as the timed CPU
+baseline. The library never calls it: there is no CPU fallback.
+
+Contents, each restating the reference (rocking5566/flash-attention-v4-rocm):
+
+* ``bf16_round`` / ``bf16_bits`` / ``from_bf16_bits``: round-to-nearest-even
+  FP32 -> BF16, the rounding ``torch.randn(..., dtype=torch.bfloat16)`` and the
+  kernel's ``T(e)`` conversions apply (src/bshd_kernel.hpp:175, :205).
+* ``inputs``: the input patterns of benchmarks/bshd.py:77-87 (normal, zero,
+  large, negative, late_max), drawn from numpy's PCG64 so they are identical
+  on every machine.
+* ``reference``: FP64 softmax(Q K^T * scale) V and logsumexp, top-left causal,
+  restating benchmarks/bshd.py:90-100 on the CPU (the reference hard-codes
+  device='cuda' and scale=1/sqrt(128); here scale is a parameter).
+* ``errors``: the reference's BF16 acceptance test (benchmarks/bshd.py:22-32)
+  plus the north-star bounds max|dO| <= 2e-2, mean|dO| <= 2e-3, |dLSE| <= 1e-3.
+* ``emulate``: a kernel-faithful FP32 emulation (tiles of 128 keys, lazy
+  rescale with threshold 8 base-2 units, P rounded to BF16, row sum over the
+  unrounded FP32 probabilities: src/bshd_kernel.hpp:148-181) that explains the
+  finite-precision behaviour of the GPU kernel. Small cases only.
+
+Parity pin: tests/golden/ holds FP64 outputs produced by the reference's own
+``reference()`` function (benchmarks/bshd.py:90-100) on these inputs; the CPU
+test suite checks this restatement against them.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+D = 128
+PATTERNS = ("normal", "zero", "large", "negative", "late_max")
+
+
+# ----------------------------------------------------------------- BF16 ----
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """FP32 -> BF16 bit patterns (uint16), round to nearest even, NaN kept."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounding = ((u >> 16) & 1) + np.uint32(0x7FFF)
+    out = ((u + rounding) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = np.uint16(0x7FC0)
+    return out
+
+
+def from_bf16_bits(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return from_bf16_bits(bf16_bits(x))
+
+
+# --------------------------------------------------------------- inputs ----
+def inputs(b: int, h: int, sq: int, sk: int, pattern: str = "normal", seed: int = 0):
+    """Q/K/V as FP32 arrays holding BF16 values, shapes [B,S,H,128].
+
+    Patterns restate benchmarks/bshd.py:77-87: ``zero`` Q=K=0; ``large`` Q,K x4;
+    ``negative`` Q=8, K=-8 (constant logit -8*8*128*scale); ``late_max`` Q=1 and
+    K rows = floor(pos/64), so logits rise every 64 keys. V is always N(0,1).
+    """
+    if pattern not in PATTERNS:
+        raise ValueError(pattern)
+    rng = np.random.default_rng(seed)
+    q = bf16_round(rng.standard_normal((b, sq, h, D), dtype=np.float32))
+    k = bf16_round(rng.standard_normal((b, sk, h, D), dtype=np.float32))
+    v = bf16_round(rng.standard_normal((b, sk, h, D), dtype=np.float32))
+    if pattern == "zero":
+        q[:] = 0
+        k[:] = 0
+    elif pattern == "large":
+        q = bf16_round(q * 4)
+        k = bf16_round(k * 4)
+    elif pattern == "negative":
+        q[:] = 8
+        k[:] = -8
+    elif pattern == "late_max":
+        q[:] = 1
+        k[:] = (np.arange(sk) // 64).astype(np.float32)[None, :, None, None]
+    return q, k, v
+
+
+def edge_inputs(seed: int = 3, b: int = 3, h: int = 5, sq: int = 1000, sk: int = 1537):
+    """The structured rescale/edge case (B3 H5 1000x1537, seed 3).
+
+    head 0-1: Q x 30 (large logits); head 2: Q gets a common direction u
+    (Q += 6u) and K rows >= 1400 are set to 4 * mean(Q) -- a late max jump of
+    well over 8 base-2 units, visible to dense rows; head 3: K constant (all
+    logits of a row equal); head 4: like head 2 with the jump at key 600, so
+    causal rows >= 600 see it too.
+    Returns (q, k, v, jumps) with jumps = {head: first key of the jump}.
+    """
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((b, sq, h, D), dtype=np.float32)
+    k = rng.standard_normal((b, sk, h, D), dtype=np.float32)
+    v = rng.standard_normal((b, sk, h, D), dtype=np.float32)
+    q[:, :, 0:2, :] *= 30.0
+    jumps = {2: 1400, 4: 600}
+    for head, pos in jumps.items():
+        u = rng.standard_normal(D).astype(np.float32)
+        u /= np.linalg.norm(u)
+        q[:, :, head, :] += 6.0 * u
+        qm = bf16_round(q[:, :, head, :]).mean(axis=(0, 1))
+        k[:, pos:, head, :] = 4.0 * qm
+    k[:, :, 3, :] = 0.5
+    return bf16_round(q), bf16_round(k), bf16_round(v), jumps
+
+
+def realised_jump_base2(q, k, head: int, pos: int, scale: float, rows=None) -> np.ndarray:
+    """Per-row increase (base-2 units) of the running max at key `pos`."""
+    qs = q[:, :, head, :].astype(np.float64) if rows is None else q[:, rows, head, :].astype(np.float64)
+    ks = k[:, :, head, :].astype(np.float64)
+    s = np.einsum("bqd,bkd->bqk", qs, ks) * scale / math.log(2.0)
+    return s[:, :, pos:].max(-1) - s[:, :, :pos].max(-1)
+
+
+# ------------------------------------------------------------ reference ----
+def sample_rows(n: int) -> np.ndarray:
+    """The rows benchmarks/bshd.py:147-148 checks at benchmark sizes."""
+    rows = {0, 1, 63, 64, 127, 128, n - 1} | set(range(0, n, max(1, n // 24)))
+    return np.array(sorted(r for r in rows if 0 <= r < n), dtype=np.int64)
+
+
+def reference(q, k, v, causal: bool, rows=None, scale: float | None = None):
+    """FP64 attention on the CPU, restating benchmarks/bshd.py:90-100.
+
+    q [B,Sq,H,128], k/v [B,Sk,H,128]; `rows` selects query rows (all if None).
+    Returns O [B,H,len(rows),128] (FP64) and LSE [B,H,len(rows)] (FP64), the
+    same [B,H,rows,...] layout as the reference's permuted result.
+    """
+    sq = q.shape[1]
+    if rows is None:
+        rows = np.arange(sq)
+    rows = np.asarray(rows, dtype=np.int64)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qs = np.ascontiguousarray(q[:, rows].transpose(0, 2, 1, 3), dtype=np.float64)
+    ks = np.ascontiguousarray(k.transpose(0, 2, 1, 3), dtype=np.float64)
+    scores = (qs @ ks.transpose(0, 1, 3, 2)) * scale
+    del qs, ks
+    if causal:
+        mask = np.arange(k.shape[1])[None, :] > rows[:, None]
+        scores[:, :, mask] = -np.inf
+    mx = scores.max(-1, keepdims=True)
+    e = np.exp(scores - mx)
+    del scores
+    ssum = e.sum(-1, keepdims=True)
+    lse = (np.log(ssum) + mx)[..., 0]
+    vs = np.ascontiguousarray(v.transpose(0, 2, 1, 3), dtype=np.float64)
+    o = (e / ssum) @ vs
+    return o, lse
+
+
+def reference_chunked(q, k, v, causal: bool, rows, scale: float | None = None, max_elems: int = 1 << 26):
+    """`reference` evaluated one (batch, head) and row chunk at a time, to bound
+    memory at long sequence lengths. Same results."""
+    b, _, h, _ = q.shape
+    rows = np.asarray(rows, dtype=np.int64)
+    o = np.empty((b, h, len(rows), D))
+    lse = np.empty((b, h, len(rows)))
+    step = max(1, max_elems // max(1, k.shape[1]))
+    for bi in range(b):
+        for hi in range(h):
+            for r0 in range(0, len(rows), step):
+                rr = rows[r0:r0 + step]
+                oo, ll = reference(q[bi:bi + 1, :, hi:hi + 1], k[bi:bi + 1, :, hi:hi + 1],
+                                   v[bi:bi + 1, :, hi:hi + 1], causal, rr, scale)
+                o[bi, hi, r0:r0 + len(rr)] = oo[0, 0]
+                lse[bi, hi, r0:r0 + len(rr)] = ll[0, 0]
+    return o, lse
+
+
+# ------------------------------------------------------------- criteria ----
+REF_TOL = dict(atol=0.01, rtol=0.01, rms=0.005, lse=2e-4)  # benchmarks/bshd.py:25 (BF16 row)
+NORTH_STAR_TOL = dict(max_abs=2e-2, mean_abs=2e-3, lse=1e-3)
+
+
+def error_stats(o, lse, ref, ref_lse) -> dict:
+    """Error statistics of O (any layout matching ref) and LSE against FP64."""
+    o = np.asarray(o, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    diff = np.abs(o - ref)
+    norm = (diff / (REF_TOL["atol"] + REF_TOL["rtol"] * np.abs(ref))).max() if diff.size else 0.0
+    rms_ref = math.sqrt(max(float(np.mean(ref * ref)) if ref.size else 0.0, 1e-60))
+    rms_rel = math.sqrt(float(np.mean(diff * diff))) / max(rms_ref, 1e-30) if diff.size else 0.0
+    out = dict(max_abs=float(diff.max()) if diff.size else 0.0, mean_abs=float(diff.mean()) if diff.size else 0.0,
+               rms_rel=float(rms_rel), max_tolerance_ratio=float(norm), finite=bool(np.isfinite(o).all()),
+               lse_max_abs=None)
+    if lse is not None:
+        out["lse_max_abs"] = float(np.abs(np.asarray(lse, dtype=np.float64) - ref_lse).max())
+    return out
+
+
+def reference_criteria_pass(o, lse, ref, ref_lse) -> bool:
+    """True iff the reference's BF16 acceptance test (benchmarks/bshd.py:22-32)
+    passes: all O finite, max |dO|/(0.01+0.01|ref|) <= 1, rms(dO)/rms(ref) <=
+    5e-3 and, when LSE is given, max |dLSE| <= 2e-4."""
+    r = error_stats(o, lse, ref, ref_lse)
+    ok = r["finite"] and r["max_tolerance_ratio"] <= 1.0 and r["rms_rel"] <= REF_TOL["rms"]
+    return bool(ok and (r["lse_max_abs"] is None or r["lse_max_abs"] <= REF_TOL["lse"]))
+
+
+def errors(o, lse, ref, ref_lse) -> dict:
+    """Assert the reference's BF16 criteria (benchmarks/bshd.py:22-32) and the
+    north-star bounds; return the statistics."""
+    r = error_stats(o, lse, ref, ref_lse)
+    assert r["finite"], r
+    assert r["max_tolerance_ratio"] <= 1.0 and r["rms_rel"] <= REF_TOL["rms"], r
+    assert r["max_abs"] <= NORTH_STAR_TOL["max_abs"] and r["mean_abs"] <= NORTH_STAR_TOL["mean_abs"], r
+    if r["lse_max_abs"] is not None:
+        assert r["lse_max_abs"] <= REF_TOL["lse"], r
+    return r
+
+
+# ------------------------------------------------------------- emulation ----
+POLY = (1.0, 0.6932829022407532, 0.2422109693288803, 0.055009059607982635)  # c0..c3 of the kernel
+
+
+def ex2_poly(x: np.ndarray) -> np.ndarray:
+    """The kernel's FMA-pipe exp2 (Cody-Waite split + cubic), in FP32."""
+    t = np.maximum(x.astype(np.float32), np.float32(-126.0))
+    j = np.rint(t).astype(np.float32)
+    f = (t - j).astype(np.float32)
+    c0, c1, c2, c3 = (np.float32(c) for c in POLY)
+    p = ((c3 * f + c2) * f + c1) * f + c0
+    y = np.ldexp(p.astype(np.float32), j.astype(np.int32)).astype(np.float32)
+    return np.where(x < np.float32(-126.0), np.float32(0.0), y).astype(np.float32)
+
+
+def emulate(q, k, v, causal: bool, scale: float | None = None, block_n: int = 128, poly_per8: int = 0,
+            kv_begin: int = 0, kv_end: int | None = None):
+    """FP32 emulation of the GPU algorithm. Returns (O bf16-valued FP32 [B,Sq,H,128],
+    LSE FP32 [B,H,Sq]); rows that see no key get O = 0 and LSE = -inf."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    b, sq, h, _ = q.shape
+    sk = k.shape[1]
+    kv_end = sk if kv_end is None else kv_end
+    scale2 = np.float32(np.float32(scale) * np.float32(1.4426950408889634))
+    o_out = np.zeros((b, sq, h, D), np.float32)
+    lse_out = np.full((b, h, sq), -np.inf, np.float32)
+    rows = np.arange(sq)
+    poly_cols = (np.arange(block_n) % 8) < poly_per8
+    for bi in range(b):
+        for hi in range(h):
+            qs = q[bi, :, hi].astype(np.float32)
+            m = np.full(sq, -np.inf, np.float32)
+            l = np.zeros(sq, np.float32)
+            acc = np.zeros((sq, D), np.float32)
+            first = True
+            for c0 in range(kv_begin, kv_end, block_n):
+                cols = np.arange(c0, min(c0 + block_n, kv_end))
+                s = (qs @ k[bi, cols, hi].astype(np.float32).T).astype(np.float32)
+                vis = np.ones_like(s, dtype=bool)
+                if causal:
+                    vis &= cols[None, :] <= rows[:, None]
+                s = np.where(vis, s, -np.inf).astype(np.float32)
+                mx = (s.max(-1) * scale2).astype(np.float32)
+                cand = np.maximum(m, mx)
+                update = np.ones(sq, bool) if first else cand > m + np.float32(8.0)
+                m_new = np.where(update, cand, m)
+                if not first:
+                    with np.errstate(invalid="ignore"):
+                        alpha = np.where(m_new == -np.inf, np.float32(1), np.exp2(m - m_new)).astype(np.float32)
+                    acc *= alpha[:, None]
+                    l *= alpha
+                m = m_new
+                mb = np.where(m == -np.inf, np.float32(0), m).astype(np.float32)
+                x = (s * scale2 - mb[:, None]).astype(np.float32)
+                p = np.exp2(x).astype(np.float32)
+                pc = poly_cols[: len(cols)]
+                if pc.any():
+                    p[:, pc] = ex2_poly(x[:, pc])
+                l = (l + p.sum(-1, dtype=np.float32)).astype(np.float32)
+                acc = (acc + bf16_round(p) @ v[bi, cols, hi].astype(np.float32)).astype(np.float32)
+                first = False
+            with np.errstate(divide="ignore", invalid="ignore"):
+                inv = np.where(l > 0, np.float32(1) / l, np.float32(0)).astype(np.float32)
+                lse = np.where(l > 0, m * np.float32(math.log(2.0)) + np.log(l), -np.inf).astype(np.float32)
+            o_out[bi, :, hi] = bf16_round(acc * inv[:, None])
+            lse_out[bi, hi] = lse
+    return o_out, lse_out

@@ -1,0 +1,131 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the public
+headers declare, lays out Fav4Args like the C compiler does, and rejects
+invalid arguments exactly as the reference does (src/bshd.hip:27-34) --
+all without touching a GPU (validation returns before any CUDA call)."""
+import ctypes as C
+import math
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+import fav4_bshd as F
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+INVALID = F.CUDA_ERROR_INVALID_VALUE
+A16 = 0x10000  # an aligned dummy address (never dereferenced: validation fails first)
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^\s*int\s+(fav4_\w+)\s*\(", text, flags=re.M)
+    return names
+
+
+def test_headers_declare_the_reference_entry_points():
+    names = declared_functions()
+    assert "fav4_bshd_forward" in names and "fav4_bshd_select_config" in names
+    assert len(names) == len(set(names))
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_declared_symbol(lib, name):
+    assert hasattr(lib, name)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(F.LIB_PATH)], capture_output=True, text=True).stdout
+    assert re.search(rf"\bT {name}$", out, flags=re.M), name
+
+
+def test_probe_library_loads():
+    p = F.load_probe_library()
+    for name in ("fav4_probe_tma_load", "fav4_probe_gemm_qk", "fav4_probe_gemm_pv", "fav4_probe_bounded_wait",
+                 "fav4_probe_status"):
+        assert hasattr(p, name)
+
+
+def test_args_layout_matches_c_compiler(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "fav4_bshd.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(Fav4Args),'
+                   'offsetof(Fav4Args,q),offsetof(Fav4Args,k),offsetof(Fav4Args,v),offsetof(Fav4Args,o),'
+                   'offsetof(Fav4Args,lse),offsetof(Fav4Args,batch),offsetof(Fav4Args,heads),'
+                   'offsetof(Fav4Args,sq),offsetof(Fav4Args,sk),offsetof(Fav4Args,scale));return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", str(src), "-o",
+                    str(exe)], check=True)
+    got = list(map(int, subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()))
+    want = [C.sizeof(F.Args)] + [getattr(F.Args, f).offset for f in
+                                 ("q", "k", "v", "o", "lse", "batch", "heads", "sq", "sk", "scale")]
+    assert got == want
+
+
+def make_args(**kw):
+    a = dict(q=A16, k=A16 * 2, v=A16 * 3, o=A16 * 4, lse=None, batch=2, heads=8, sq=64, sk=64,
+             scale=1 / math.sqrt(128))
+    a.update(kw)
+    return F.Args(a["q"], a["k"], a["v"], a["o"], a["lse"], a["batch"], a["heads"], a["sq"], a["sk"], a["scale"])
+
+
+INVALID_CASES = [
+    dict(q=None), dict(k=None), dict(v=None), dict(o=None),
+    dict(batch=0), dict(heads=0), dict(sq=0), dict(sk=0), dict(batch=-1), dict(sq=-5),
+    dict(scale=0.0), dict(scale=-1.0), dict(scale=float("nan")), dict(scale=float("inf")),
+    dict(q=A16 + 8), dict(k=A16 + 2), dict(v=A16 + 1), dict(o=A16 + 4),
+    dict(batch=2 ** 20, heads=2 ** 12),                  # batch*heads overflows INT_MAX
+    dict(heads=2 ** 24 + 1),                              # heads*128 overflows
+    dict(heads=64, sq=2 ** 18 + 1),                       # sq*heads*128 overflows
+    dict(heads=64, sk=2 ** 18 + 1),                       # sk*heads*128 overflows
+]
+
+
+@pytest.mark.parametrize("kw", INVALID_CASES, ids=[str(c) for c in INVALID_CASES])
+def test_forward_rejects_invalid_arguments(lib, kw):
+    a = make_args(**kw)
+    assert lib.fav4_bshd_forward(C.byref(a), 0, 0, None) == INVALID
+    assert lib.fav4_bshd_forward(C.byref(a), 1, 2, None) == INVALID
+
+
+@pytest.mark.parametrize("causal,config", [(2, 0), (-1, 0), (0, 4), (0, -1), (1, 7)])
+def test_forward_rejects_bad_mode_or_config(lib, causal, config):
+    a = make_args()
+    assert lib.fav4_bshd_forward(C.byref(a), causal, config, None) == INVALID
+
+
+def test_forward_rejects_null_args(lib):
+    assert lib.fav4_bshd_forward(None, 0, 0, None) == INVALID
+
+
+def test_select_config_auto_rule(lib):
+    # reference src/bshd.hip:23-25: sq < 128 -> 1, else 2
+    for sq, want in ((1, 1), (127, 1), (128, 2), (4096, 2)):
+        a = make_args(sq=sq)
+        assert lib.fav4_bshd_select_config(C.byref(a)) == want
+
+
+@pytest.mark.parametrize("kv", [(-1, 10), (10, 10), (20, 10), (0, 65)])
+def test_partial_rejects_bad_kv_range(lib, kv):
+    a = make_args(lse=A16 * 5)
+    assert lib.fav4_bshd_forward_partial(C.byref(a), 1, 0, kv[0], kv[1], None) == INVALID
+
+
+def test_partial_requires_lse(lib):
+    a = make_args(lse=None)
+    assert lib.fav4_bshd_forward_partial(C.byref(a), 0, 0, 0, 64, None) == INVALID
+    a = make_args(lse=A16 * 5 + 2)
+    assert lib.fav4_bshd_forward_partial(C.byref(a), 0, 0, 0, 64, None) == INVALID
+
+
+def test_combine_rejects_invalid_arguments(lib):
+    o = (C.c_void_p * 2)(A16, A16 * 2)
+    lse = (C.c_void_p * 2)(A16 * 3, A16 * 4)
+    f = lib.fav4_bshd_combine
+    assert f(o, lse, 0, A16 * 5, None, 1, 8, 64, None) == INVALID        # no parts
+    assert f(o, lse, 17, A16 * 5, None, 1, 8, 64, None) == INVALID       # too many
+    assert f(o, lse, 2, None, None, 1, 8, 64, None) == INVALID           # no output
+    assert f(o, lse, 2, A16 * 5 + 8, None, 1, 8, 64, None) == INVALID    # misaligned output
+    assert f(o, lse, 2, A16 * 5, None, 0, 8, 64, None) == INVALID        # empty batch
+    bad = (C.c_void_p * 2)(A16, None)
+    assert f(bad, lse, 2, A16 * 5, None, 1, 8, 64, None) == INVALID      # null part
