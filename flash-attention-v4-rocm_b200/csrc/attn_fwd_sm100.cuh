@@ -35,6 +35,9 @@ constexpr int kBoxBytes = 128 * 64 * 2;          // one TMA box: 128 rows x 64 b
 constexpr int kTileBytes = 2 * kBoxBytes;        // a 128 x 128 bf16 tile = 32 KiB
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;        // base-2 units, bshd_kernel.hpp:157
+constexpr uint32_t kLaunchRegs = 168;            // 65536 / 384 rounded down to a multiple of 8
+constexpr uint32_t kSoftmaxRegs = 216;
+constexpr uint32_t kOtherRegs = 72;
 
 struct FwdParams {
   __nv_bfloat16* o;
@@ -133,11 +136,64 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return x < -126.0f ? 0.0f : y;
 }
 
-// Columns c with (c % 8) < PolyPer8 use the polynomial, the rest MUFU ex2.
-template <int PolyPer8>
-__device__ __forceinline__ float ex2_split(float x, int c) {
-  if (PolyPer8 > 0 && (c % 8) < PolyPer8) return ex2_poly(x);
-  return ex2_mufu(x);
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// The polynomial exp2 on a pair, with packed FP32x2 FMA-pipe arithmetic.
+// Exact0: inputs below -126 (masked keys are -inf) give exactly 0; without it
+// they give ~2^-126 * p(f) (only reachable from logits 126 base-2 units under
+// the row maximum, where the true value is 0 to FP32 precision anyway).
+template <bool Exact0>
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  const float2 t = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const float2 r = __fadd2_rn(t, make_float2(12582912.0f, 12582912.0f));
+  const float2 j = __fadd2_rn(r, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), t);  // t - j, exact
+  float2 q = __ffma2_rn(make_float2(kPolyC3, kPolyC3), f, make_float2(kPolyC2, kPolyC2));
+  q = __ffma2_rn(q, f, make_float2(kPolyC1, kPolyC1));
+  q = __ffma2_rn(q, f, make_float2(1.0f, 1.0f));
+  float2 y;
+  y.x = __uint_as_float(__float_as_uint(q.x) + (__float_as_uint(r.x) << 23));
+  y.y = __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(r.y) << 23));
+  if (Exact0) {
+    y.x = x.x < -126.0f ? 0.0f : y.x;
+    y.y = x.y < -126.0f ? 0.0f : y.y;
+  }
+  return y;
+}
+
+// P = exp2(S * scale_log2 - mb) for one row of 128 scores: columns c with
+// (c % 8) < PolyPer8 use the polynomial, the rest MUFU ex2. P is rounded to
+// BF16 pairs and stored to TMEM at t_p (64 columns); the return value is the
+// row sum of the unrounded FP32 probabilities (bshd_kernel.hpp:165-181).
+template <int PolyPer8, bool Masked>
+__device__ __forceinline__ float exp_pack_store(const float (&s)[128], float scale_log2, float mb, uint32_t t_p) {
+  const float2 sc = make_float2(scale_log2, scale_log2);
+  const float2 nb = make_float2(-mb, -mb);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int cc = 0; cc < 64; cc += 2) {
+      const int c = half * 64 + cc;
+      const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sc, nb);
+      float2 e;
+      if (PolyPer8 > 0 && (c % 8) < PolyPer8) {
+        e = ex2_poly2<Masked>(x);
+      } else {
+        e = make_float2(ex2_mufu(x.x), ex2_mufu(x.y));
+      }
+      acc[(cc / 2) % 4] = __fadd2_rn(acc[(cc / 2) % 4], e);
+      pk[cc / 2] = pack_bf16x2(e.x, e.y);
+    }
+    tmem_st32(t_p + half * 32, pk);
+  }
+  const float2 a = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+  return a.x + a.y;
 }
 
 // ---------------------------------------------------------------------------
@@ -189,7 +245,15 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 8) {
+  // 384 threads launched with kLaunchRegs registers each (ptxas must report
+  // exactly that: __launch_bounds__(384, 1) caps it at 168). Softmax
+  // warpgroups take kSoftmaxRegs, the load/MMA warpgroup keeps kOtherRegs:
+  // 128 * (2 * 216 + 72) = 64512 = 384 * 168.
+  static_assert(128 * (2 * kSoftmaxRegs + kOtherRegs) <= 384 * kLaunchRegs, "register split exceeds the launch");
+
+  if (warp >= 8) {
+    regs_release<kOtherRegs>();
+    if (warp == 8) {
     // ============================ TMA producer ============================
     if (lane == 0) {
       const uint64_t pol_kv = policy_evict_last();
@@ -340,8 +404,10 @@ __global__ void __launch_bounds__(384, 1)
       mbar_wait(bar(L::kTeardown), 0, drain, kStatusTimeoutDrain);
     }
     __syncwarp();
+    }  // warps 10-11: idle
   } else if (warp < 4 * QTiles) {
     // ============================== softmax ===============================
+    regs_claim<kSoftmaxRegs>();
     const int i = warp / 4;                  // Q tile served by this warpgroup
     const int row = (warp % 4) * 32 + lane;  // TMEM lane = row within the Q tile
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
@@ -372,55 +438,49 @@ __global__ void __launch_bounds__(384, 1)
         for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c / 32][c % 32]);
         const int col0 = p.kv_begin + j * kBlockN;
         // Mask keys past kv_end, and (causal) keys after this row.
-        const bool tail = col0 + kBlockN > p.kv_end;
-        const bool diag = Causal && (col0 + kBlockN - 1 > r0);
-        if (tail || diag) {
+        const bool masked = (col0 + kBlockN > p.kv_end) || (Causal && (col0 + kBlockN - 1 > r0));
+        if (masked) {
           int lim = p.kv_end - 1 - col0;  // last visible column index within the tile
           if (Causal) lim = min(lim, grow - col0);
 #pragma unroll
           for (int c = 0; c < 128; ++c) s[c] = c > lim ? -INFINITY : s[c];
         }
-        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+        float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
 #pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-          mx0 = fmaxf(mx0, fmaxf(s[c], s[c + 1]));
-          mx1 = fmaxf(mx1, fmaxf(s[c + 2], s[c + 3]));
+        for (int c = 6; c < 126; c += 4) {
+          mx0 = fmax3(mx0, s[c], s[c + 1]);
+          mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
         }
-        const float mx = fmaxf(mx0, mx1) * scale_log2;
+        const float mx = fmax3(mx0, mx1, fmaxf(s[126], s[127])) * scale_log2;
         const float cand = fmaxf(m, mx);
         const bool update = (j == 0) || (cand > m + kRescaleThreshold);
         const float m_new = update ? cand : m;
-        if (j > 0 && __any_sync(0xffffffffu, update)) {
-          // Lazy correction: O_i (which already holds P V of the previous
-          // tiles) is rescaled in TMEM by the row owner.
-          const float alpha = (m_new == -INFINITY) ? 1.f : ex2_mufu(m - m_new);
-          l *= alpha;
-#pragma unroll
+        const bool rescale = (j > 0) && __any_sync(0xffffffffu, update);
+        const float alpha = rescale ? ((m_new == -INFINITY) ? 1.f : ex2_mufu(m - m_new)) : 1.f;
+        m = m_new;
+        const float mb = (m == -INFINITY) ? 0.f : m;
+        const float rowsum = masked ? exp_pack_store<PolyPer8, true>(s, scale_log2, mb, t_s)
+                                    : exp_pack_store<PolyPer8, false>(s, scale_log2, mb, t_s);
+        l = l * alpha + rowsum;
+        if (rescale) {
+          // Lazy correction: O_i already holds P V of the previous tiles (the
+          // S commit that released this tile covers that PV); the row owner
+          // rescales it in TMEM before PV of this tile is issued.
+          const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t orow[32];
             tmem_ld32(t_o + c * 32, orow);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
+            for (int e = 0; e < 32; e += 2) {
+              const float2 v = __fmul2_rn(make_float2(__uint_as_float(orow[e]), __uint_as_float(orow[e + 1])), a2);
+              orow[e] = __float_as_uint(v.x);
+              orow[e + 1] = __float_as_uint(v.y);
+            }
             tmem_st32(t_o + c * 32, orow);
           }
         }
-        m = m_new;
-        const float mb = (m == -INFINITY) ? 0.f : m;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[2][32];
-#pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float x0 = __fmaf_rn(s[c], scale_log2, -mb);
-          const float x1 = __fmaf_rn(s[c + 1], scale_log2, -mb);
-          const float e0 = ex2_split<PolyPer8>(x0, c);
-          const float e1 = ex2_split<PolyPer8>(x1, c + 1);
-          acc[(c / 2) % 4] += e0 + e1;
-          pk[c / 64][(c % 64) / 2] = pack_bf16x2(e0, e1);
-        }
-        l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
-        tmem_st32(t_s, pk[0]);
-        tmem_st32(t_s + 32, pk[1]);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(L::kPFull + i));
@@ -465,6 +525,8 @@ __global__ void __launch_bounds__(384, 1)
             l > 0.f ? m * kLn2 + logf(l) : -INFINITY;
       }
     }
+  } else {
+    regs_release<kOtherRegs>();  // warps 4-7 when QTiles == 1: Q tile 1 unused
   }
 
   tc_fence_before();
