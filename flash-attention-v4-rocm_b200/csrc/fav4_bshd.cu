@@ -192,6 +192,75 @@ extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const*
   return cudaGetLastError();
 }
 
+// --------------------------------------------------------------------------
+// Split-KV forward with its partials in a fixed device array (no cudaMalloc),
+// for callers that cannot allocate device memory. One array per device,
+// shared by every call: overlapping calls race (see include/fav4_bshd.h).
+namespace fav4 {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(64) << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_splitkv_scratch[kStaticScratchBytes];
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// Device address of g_splitkv_scratch on the current device, looked up once
+// per device with that device current (host code cannot use the symbol itself).
+cudaError_t static_scratch(int dev, unsigned char** out) {
+  static std::mutex mu;
+  static unsigned char* addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_splitkv_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_forward_splitkv_static(const Fav4Args* a, int causal, int config, int splits,
+                                                cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || splits < 1 || splits > fav4::kMaxCombineParts)
+    return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  // Whole 128-key tiles per slice.
+  const int per = (a->sk + splits - 1) / splits;
+  const int step = ((per + fav4::kBlockN - 1) / fav4::kBlockN) * fav4::kBlockN;
+  const int parts = (a->sk + step - 1) / step;
+  const size_t rows = static_cast<size_t>(a->batch) * a->sq * a->heads;
+  const size_t o_bytes = fav4::round256(rows * fav4::kHeadDim * 2);
+  const size_t lse_bytes = fav4::round256(rows * 4);
+  if (static_cast<size_t>(parts) * (o_bytes + lse_bytes) > fav4::kStaticScratchBytes)
+    return cudaErrorMemoryAllocation;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  unsigned char* scratch = nullptr;
+  e = fav4::static_scratch(dev, &scratch);
+  if (e != cudaSuccess) return e;
+  const void* o_parts[fav4::kMaxCombineParts];
+  const float* lse_parts[fav4::kMaxCombineParts];
+  for (int g = 0; g < parts; ++g) {
+    Fav4Args pa = *a;
+    pa.o = scratch + g * o_bytes;
+    pa.lse = reinterpret_cast<float*>(scratch + parts * o_bytes + g * lse_bytes);
+    const int kv_begin = g * step;
+    const int kv_end = kv_begin + step < a->sk ? kv_begin + step : a->sk;
+    e = static_cast<cudaError_t>(causal ? fav4::dispatch<true>(pa, config, kv_begin, kv_end, stream)
+                                        : fav4::dispatch<false>(pa, config, kv_begin, kv_end, stream));
+    if (e != cudaSuccess) return e;
+    o_parts[g] = pa.o;
+    lse_parts[g] = pa.lse;
+  }
+  return fav4_bshd_combine(o_parts, lse_parts, parts, a->o, a->lse, a->batch, a->heads, a->sq, stream);
+}
+
 extern "C" int fav4_bshd_pipeline_status(int clear) {
   uint32_t v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;

@@ -42,6 +42,8 @@ def _bind(lib):
     lib.fav4_bshd_combine.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int, C.c_void_p,
                                       C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_combine.restype = C.c_int
+    lib.fav4_bshd_forward_splitkv_static.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_forward_splitkv_static.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
     lib.fav4_bshd_pipeline_status.restype = C.c_int
     return lib
