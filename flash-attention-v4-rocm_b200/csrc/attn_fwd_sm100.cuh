@@ -3,8 +3,8 @@
 // Replaces the reference's single fused kernel `bshd_kernel`
 // (src/bshd_kernel.hpp:50-211) with a warp-specialised tcgen05 pipeline:
 //
-//   warp 8  (load)     TMA: Q tiles once per work tile, then a K/V ring
-//                      (K0,V0,K1,V1,...) through STAGES 32 KiB slots.
+//   warp 8  (load)     TMA: Q tiles once per work tile, then a ring of K/V
+//                      pairs (one 64 KiB slot holds K_j and V_j).
 //   warp 9  (mma)      one thread issues tcgen05.mma: S_i = Q_i K^T into TMEM,
 //                      O_i += P_i V with P_i read back from TMEM.
 //   warps 0-3 / 4-7    softmax for Q tile 0 / Q tile 1: one TMEM lane (= one
@@ -83,29 +83,33 @@ __device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int r0) {
   return (hi - p.kv_begin + kBlockN - 1) / kBlockN;
 }
 
-template <int Stages>
+// Shared memory: Q tiles, then a ring of K/V pairs (K_j at +0, V_j at +32 KiB
+// of a 64 KiB slot; one full and one empty barrier per slot), then barriers.
+template <int QTiles, int Pairs>
 struct SmemLayout {
-  static constexpr int kQ = 0;                               // QTILES x 32 KiB (always room for 2)
-  static constexpr int kKV = 2 * kTileBytes;                 // Stages x 32 KiB
-  static constexpr int kBar = kKV + Stages * kTileBytes;     // mbarriers
+  static constexpr int kPairBytes = 2 * kTileBytes;
+  static constexpr int kQ = 0;                                // QTiles x 32 KiB
+  static constexpr int kKV = QTiles * kTileBytes;             // Pairs x 64 KiB
+  static constexpr int kBar = kKV + Pairs * kPairBytes;       // mbarriers
   // barrier slots (8 bytes each)
-  static constexpr int kQFull = 0, kQEmpty = 1, kKVFull = 2, kKVEmpty = 2 + Stages;
-  static constexpr int kSFull = 2 + 2 * Stages, kPFull = kSFull + 2, kOFull = kPFull + 2, kOEmpty = kOFull + 2;
-  static constexpr int kNumBars = kOEmpty + 2 + 1;           // + teardown barrier
+  static constexpr int kQFull = 0, kQEmpty = 1, kKVFull = 2, kKVEmpty = 2 + Pairs;
+  static constexpr int kSFull = 2 + 2 * Pairs, kPFull = kSFull + 2, kOFull = kPFull + 2, kOEmpty = kOFull + 2;
+  static constexpr int kNumBars = kOEmpty + 2 + 1;            // + teardown barrier
   static constexpr int kTeardown = kNumBars - 1;
   static constexpr int kTmemHolder = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemHolder + 4;
   static constexpr int kBytes = kAbort + 4;
-  static constexpr int kAlloc = kBytes + 1024;               // slack for 1 KiB alignment
+  static constexpr int kAlloc = kBytes + 1024;                // slack for 1 KiB alignment
+  static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
 
 // Ring position shared by the producer (load warp) and consumer (mma warp).
 struct Ring {
   int stage = 0;
   uint32_t phase = 0;
-  template <int Stages>
+  template <int Slots>
   __device__ __forceinline__ void advance() {
-    if (++stage == Stages) { stage = 0; phase ^= 1u; }
+    if (++stage == Slots) { stage = 0; phase ^= 1u; }
   }
 };
 
@@ -197,11 +201,11 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 }
 
 // ---------------------------------------------------------------------------
-template <bool Causal, int QTiles, int Stages, int PolyPer8>
+template <bool Causal, int QTiles, int Pairs, int PolyPer8>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using L = SmemLayout<Stages>;
+  using L = SmemLayout<QTiles, Pairs>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(384, 1)
     *abort_flag = 0u;
     mbar_init(bar(L::kQFull), 1);
     mbar_init(bar(L::kQEmpty), 1);
-    for (int s = 0; s < Stages; ++s) {
+    for (int s = 0; s < Pairs; ++s) {
       mbar_init(bar(L::kKVFull + s), 1);
       mbar_init(bar(L::kKVEmpty + s), 1);
     }
@@ -281,22 +285,20 @@ __global__ void __launch_bounds__(384, 1)
         }
         for (int j = 0; j < N && ok; ++j) {
           const int s0 = p.kv_begin + j * kBlockN;
-#pragma unroll 1
-          for (int which = 0; which < 2; ++which) {
-            if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
-              ok = false;
-              break;
-            }
-            const uint32_t fb = bar(L::kKVFull + ring.stage);
-            mbar_arrive_expect_tx(fb, kTileBytes);
-            armed_mask |= 1u << ring.stage;
-            armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
-            const uint32_t dst = sbase + L::kKV + ring.stage * kTileBytes;
-            const CUtensorMap* m = which == 0 ? &tm_k : &tm_v;
-            tma_load_4d(dst, m, fb, 0, tc.h, s0, tc.b, pol_kv);
-            tma_load_4d(dst + kBoxBytes, m, fb, 64, tc.h, s0, tc.b, pol_kv);
-            ring.advance<Stages>();
+          if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
+            ok = false;
+            break;
           }
+          const uint32_t fb = bar(L::kKVFull + ring.stage);
+          mbar_arrive_expect_tx(fb, L::kPairBytes);
+          armed_mask |= 1u << ring.stage;
+          armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
+          const uint32_t dst = sbase + L::kKV + ring.stage * L::kPairBytes;
+          tma_load_4d(dst, &tm_k, fb, 0, tc.h, s0, tc.b, pol_kv);
+          tma_load_4d(dst + kBoxBytes, &tm_k, fb, 64, tc.h, s0, tc.b, pol_kv);
+          tma_load_4d(dst + kTileBytes, &tm_v, fb, 0, tc.h, s0, tc.b, pol_kv);
+          tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_v, fb, 64, tc.h, s0, tc.b, pol_kv);
+          ring.advance<Pairs>();
         }
       }
       if (!ok) {
@@ -304,37 +306,49 @@ __global__ void __launch_bounds__(384, 1)
         WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
         volatile uint32_t no_abort = 0;
         drain.abort = &no_abort;
-        for (int s = 0; s < Stages; ++s)
+        for (int s = 0; s < Pairs; ++s)
           if (armed_mask & (1u << s)) mbar_wait(bar(L::kKVFull + s), (armed_par >> s) & 1u, drain, kStatusTimeoutDrain);
       }
     }
     __syncwarp();
   } else if (warp == 9) {
     // ============================= MMA issuer =============================
+    // One thread issues every MMA, in the order S0(0) S1(0), then per K/V
+    // pair j: PV0(j) S0(j+1) PV1(j) S1(j+1). That order makes the two Q tiles
+    // ping-pong (softmax of one tile overlaps the other tile's MMAs), and since
+    // tcgen05 ops of one thread execute in issue order, S_i(j+1) overwrites
+    // P_i only after PV_i(j) has read it.
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kBlockM, kBlockN, false);
       constexpr uint32_t idesc_pv = make_idesc_bf16(kBlockM, kHeadDim, true);
       Ring ring;
       uint32_t q_full_par = 0, p_par[2] = {0, 0}, o_empty_par[2] = {1, 1};
       bool ok = true;
-      auto issue_s = [&](int i, int kstage) {
-        const uint32_t qa = sbase + L::kQ + i * kTileBytes;
-        const uint32_t ka = sbase + L::kKV + kstage * kTileBytes;
+      // Descriptor words, computed once: K-major (Q, K) and MN-major (V),
+      // 128-byte swizzle, 8-row groups 1024 bytes apart; V's two 64-column
+      // halves are one box (16 KiB) apart. Per MMA only the address word moves.
+      const uint64_t dk = make_sdesc_sw128(sbase, 16, 1024);
+      const uint64_t dv = make_sdesc_sw128(sbase, kBoxBytes, 1024);
+      const uint32_t k_lo = static_cast<uint32_t>(dk), k_hi = static_cast<uint32_t>(dk >> 32);
+      const uint32_t v_lo = static_cast<uint32_t>(dv), v_hi = static_cast<uint32_t>(dv >> 32);
+      auto issue_s = [&](int i, int slot) {
+        const uint32_t qa = k_lo + ((L::kQ + i * kTileBytes) >> 4);
+        const uint32_t ka = k_lo + ((L::kKV + slot * L::kPairBytes) >> 4);
+        const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int k = 0; k < kHeadDim / 16; ++k) {
-          const uint32_t off = (k / 4) * kBoxBytes + (k % 4) * 32;
-          umma_ss(tmem + i * 128, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(ka + off, 16, 1024),
-                  idesc_qk, k > 0 ? 1u : 0u);
+          const uint32_t off = ((k / 4) * kBoxBytes + (k % 4) * 32) >> 4;
+          umma_ss_w(d, qa + off, k_hi, ka + off, k_hi, idesc_qk, k > 0 ? 1u : 0u);
         }
         tc_commit(bar(L::kSFull + i));
       };
-      auto issue_pv = [&](int i, int vstage, bool acc) {
-        const uint32_t va = sbase + L::kKV + vstage * kTileBytes;
+      auto issue_pv = [&](int i, int slot, bool acc) {
+        const uint32_t va = v_lo + ((L::kKV + slot * L::kPairBytes + kTileBytes) >> 4);
+        const uint32_t d = tmem + 256 + i * 128;
+        const uint32_t pa = tmem + i * 128;
+        umma_ts_w(d, pa, va, v_hi, idesc_pv, acc ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < kBlockN / 16; ++k) {
-          umma_ts(tmem + 256 + i * 128, tmem + i * 128 + k * 8, make_sdesc_sw128(va + k * 2048, kBoxBytes, 1024),
-                  idesc_pv, (acc || k > 0) ? 1u : 0u);
-        }
+        for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
       };
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
@@ -344,56 +358,42 @@ __global__ void __launch_bounds__(384, 1)
         if (N == 0) continue;
         if (!mbar_wait(bar(L::kQFull), q_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
         q_full_par ^= 1u;
-        // K(0)
-        int kstage = ring.stage;
-        if (!mbar_wait(bar(L::kKVFull + kstage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
-        ring.advance<Stages>();
+        if (!mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        if (n0 > 0) issue_s(0, kstage);
-        if (n1 > 0) issue_s(1, kstage);
-        tc_commit(bar(L::kKVEmpty + kstage));
+        if (n0 > 0) issue_s(0, ring.stage);
+        if (n1 > 0) issue_s(1, ring.stage);
         if (N == 1) tc_commit(bar(L::kQEmpty));
         for (int j = 0; j < N && ok; ++j) {
-          const int vstage = ring.stage;
-          if (!mbar_wait(bar(L::kKVFull + vstage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
-          ring.advance<Stages>();
-          const bool next_k = j + 1 < N;
-          int nk_stage = -1;
-          uint32_t nk_phase = 0;
-          bool nk_ready = false;
-          if (next_k) {
-            nk_stage = ring.stage;
-            nk_phase = ring.phase;
-            ring.advance<Stages>();
-          }
-#pragma unroll 1
+          const int cur = ring.stage;
+          Ring nxt = ring;
+          nxt.advance<Pairs>();
+          bool next_ready = false;
+#pragma unroll
           for (int i = 0; i < QTiles; ++i) {
             const int ni = i == 0 ? n0 : n1;
-            if (j >= ni) continue;
-            if (!mbar_wait(bar(L::kPFull + i), p_par[i], ctl, kStatusTimeoutMma)) { ok = false; break; }
+            if (j >= ni || !ok) continue;
+            if (!mbar_wait(bar(L::kPFull + i), p_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
             p_par[i] ^= 1u;
             if (j == 0) {
-              if (!mbar_wait(bar(L::kOEmpty + i), o_empty_par[i], ctl, kStatusTimeoutMma)) { ok = false; break; }
+              if (!mbar_wait(bar(L::kOEmpty + i), o_empty_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
               o_empty_par[i] ^= 1u;
             }
             tc_fence_after();
-            issue_pv(i, vstage, j > 0);
+            issue_pv(i, cur, j > 0);
             if (j + 1 == ni) tc_commit(bar(L::kOFull + i));
             if (j + 1 < ni) {
-              if (!nk_ready) {
-                if (!mbar_wait(bar(L::kKVFull + nk_stage), nk_phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
-                nk_ready = true;
+              if (!next_ready) {
+                if (!mbar_wait(bar(L::kKVFull + nxt.stage), nxt.phase, ctl, kStatusTimeoutMma)) { ok = false; continue; }
+                next_ready = true;
                 tc_fence_after();
               }
-              issue_s(i, nk_stage);
+              issue_s(i, nxt.stage);
             }
           }
           if (!ok) break;
-          tc_commit(bar(L::kKVEmpty + vstage));
-          if (next_k) {
-            tc_commit(bar(L::kKVEmpty + nk_stage));
-            if (j + 2 == N) tc_commit(bar(L::kQEmpty));
-          }
+          tc_commit(bar(L::kKVEmpty + cur));  // K(j) and V(j) are no longer read
+          if (j + 2 == N) tc_commit(bar(L::kQEmpty));
+          ring = nxt;
         }
       }
       // Every MMA this thread issued has finished once this barrier flips.
@@ -445,13 +445,19 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int c = 0; c < 128; ++c) s[c] = c > lim ? -INFINITY : s[c];
         }
+        // four independent max chains (the latency of one 64-long chain shows)
         float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+        float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-        for (int c = 6; c < 126; c += 4) {
+        for (int c = 12; c < 124; c += 8) {
           mx0 = fmax3(mx0, s[c], s[c + 1]);
           mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+          mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+          mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
         }
-        const float mx = fmax3(mx0, mx1, fmaxf(s[126], s[127])) * scale_log2;
+        mx0 = fmax3(mx0, s[124], s[125]);
+        mx1 = fmax3(mx1, s[126], s[127]);
+        const float mx = fmax3(fmaxf(mx0, mx1), mx2, mx3) * scale_log2;
         const float cand = fmaxf(m, mx);
         const bool update = (j == 0) || (cand > m + kRescaleThreshold);
         const float m_new = update ? cand : m;

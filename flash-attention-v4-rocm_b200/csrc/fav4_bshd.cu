@@ -79,19 +79,19 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 }
 
 // B200 tilings behind the reference's config ids (include/fav4_bshd.h:17-18):
-//   1: one 128-row Q tile per CTA, 4-stage K/V ring, MUFU exp2 only
-//   2: two 128-row Q tiles per CTA sharing each K/V tile, 3-stage ring,
-//      1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
-//   3: two Q tiles, 4-stage ring, 1/2 of exp2 on the polynomial
-template <bool Causal, int QTiles, int Stages, int PolyPer8>
+//   1: one 128-row Q tile per CTA, 3 K/V pair slots, MUFU exp2 only
+//   2: two 128-row Q tiles per CTA sharing each K/V pair (ping-pong),
+//      2 pair slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
+//   3: as 2 with 1/2 of exp2 on the polynomial
+template <bool Causal, int QTiles, int Pairs, int PolyPer8>
 int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   DeviceInfo info;
   if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
-  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Stages, PolyPer8>;
-  constexpr int smem = SmemLayout<Stages>::kAlloc;
+  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Pairs, PolyPer8>;
+  constexpr int smem = SmemLayout<QTiles, Pairs>::kAlloc;
   {
     static std::mutex mu;
     static bool attr_set[kMaxDevices] = {};
@@ -130,9 +130,9 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
 template <bool Causal>
 int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream) {
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 4, 0>(a, kv_begin, kv_end, stream);
-    case 2: return launch_fwd<Causal, 2, 3, 2>(a, kv_begin, kv_end, stream);
-    case 3: return launch_fwd<Causal, 2, 4, 4>(a, kv_begin, kv_end, stream);
+    case 1: return launch_fwd<Causal, 1, 3, 0>(a, kv_begin, kv_end, stream);
+    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_begin, kv_end, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_begin, kv_end, stream);
     default: return cudaErrorInvalidValue;
   }
 }
