@@ -3,8 +3,8 @@
 // Replaces the reference's single fused kernel `bshd_kernel`
 // (src/bshd_kernel.hpp:50-211) with a warp-specialised tcgen05 pipeline:
 //
-//   warp 8  (load)     TMA: Q tiles once per work tile, then a ring of K/V
-//                      pairs (one 64 KiB slot holds K_j and V_j).
+//   warp 8  (load)     TMA: Q tiles once per work tile, then a ring of 64 KiB
+//                      slots holding the groups {K0}, {V0,K1}, {V1,K2}, ...
 //   warp 9  (mma)      one thread issues tcgen05.mma: S_i = Q_i K^T into TMEM,
 //                      O_i += P_i V with P_i read back from TMEM.
 //   warps 0-3 / 4-7    softmax for Q tile 0 / Q tile 1: one TMEM lane (= one
@@ -83,17 +83,20 @@ __device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int r0) {
   return (hi - p.kv_begin + kBlockN - 1) / kBlockN;
 }
 
-// Shared memory: Q tiles, then a ring of K/V pairs (K_j at +0, V_j at +32 KiB
-// of a 64 KiB slot; one full and one empty barrier per slot), then barriers.
-template <int QTiles, int Pairs>
+// Shared memory: Q tiles, then a ring of 64 KiB slots, then barriers. Per work
+// tile the load warp fills the ring with the groups G(-1) = {K0},
+// G(j) = {V_j, K_j+1} (j = 0..N-2) and G(N-1) = {V_N-1}: exactly what the MMA
+// warp consumes in its prologue (S(0)) and in step j (PV(j), S(j+1)). V sits
+// at +0 and K at +32 KiB of a slot; one full and one empty barrier per slot.
+template <int QTiles, int Slots>
 struct SmemLayout {
-  static constexpr int kPairBytes = 2 * kTileBytes;
+  static constexpr int kSlotBytes = 2 * kTileBytes;
   static constexpr int kQ = 0;                                // QTiles x 32 KiB
-  static constexpr int kKV = QTiles * kTileBytes;             // Pairs x 64 KiB
-  static constexpr int kBar = kKV + Pairs * kPairBytes;       // mbarriers
+  static constexpr int kKV = QTiles * kTileBytes;             // Slots x 64 KiB
+  static constexpr int kBar = kKV + Slots * kSlotBytes;       // mbarriers
   // barrier slots (8 bytes each)
-  static constexpr int kQFull = 0, kQEmpty = 1, kKVFull = 2, kKVEmpty = 2 + Pairs;
-  static constexpr int kSFull = 2 + 2 * Pairs, kPFull = kSFull + 2, kOFull = kPFull + 2, kOEmpty = kOFull + 2;
+  static constexpr int kQFull = 0, kQEmpty = 1, kKVFull = 2, kKVEmpty = 2 + Slots;
+  static constexpr int kSFull = 2 + 2 * Slots, kPFull = kSFull + 2, kOFull = kPFull + 2, kOEmpty = kOFull + 2;
   static constexpr int kNumBars = kOEmpty + 2 + 1;            // + teardown barrier
   static constexpr int kTeardown = kNumBars - 1;
   static constexpr int kTmemHolder = kBar + kNumBars * 8;
@@ -201,11 +204,11 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 }
 
 // ---------------------------------------------------------------------------
-template <bool Causal, int QTiles, int Pairs, int PolyPer8>
+template <bool Causal, int QTiles, int Slots, int PolyPer8>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using L = SmemLayout<QTiles, Pairs>;
+  using L = SmemLayout<QTiles, Slots>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(384, 1)
     *abort_flag = 0u;
     mbar_init(bar(L::kQFull), 1);
     mbar_init(bar(L::kQEmpty), 1);
-    for (int s = 0; s < Pairs; ++s) {
+    for (int s = 0; s < Slots; ++s) {
       mbar_init(bar(L::kKVFull + s), 1);
       mbar_init(bar(L::kKVEmpty + s), 1);
     }
@@ -283,22 +286,28 @@ __global__ void __launch_bounds__(384, 1)
           tma_load_4d(dst, &tm_q, bar(L::kQFull), 0, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
           tma_load_4d(dst + kBoxBytes, &tm_q, bar(L::kQFull), 64, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
         }
-        for (int j = 0; j < N && ok; ++j) {
-          const int s0 = p.kv_begin + j * kBlockN;
+        for (int g = -1; g < N && ok; ++g) {
           if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
             ok = false;
             break;
           }
+          const bool has_v = g >= 0, has_k = g + 1 < N;
           const uint32_t fb = bar(L::kKVFull + ring.stage);
-          mbar_arrive_expect_tx(fb, L::kPairBytes);
+          mbar_arrive_expect_tx(fb, (has_v ? kTileBytes : 0) + (has_k ? kTileBytes : 0));
           armed_mask |= 1u << ring.stage;
           armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
-          const uint32_t dst = sbase + L::kKV + ring.stage * L::kPairBytes;
-          tma_load_4d(dst, &tm_k, fb, 0, tc.h, s0, tc.b, pol_kv);
-          tma_load_4d(dst + kBoxBytes, &tm_k, fb, 64, tc.h, s0, tc.b, pol_kv);
-          tma_load_4d(dst + kTileBytes, &tm_v, fb, 0, tc.h, s0, tc.b, pol_kv);
-          tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_v, fb, 64, tc.h, s0, tc.b, pol_kv);
-          ring.advance<Pairs>();
+          const uint32_t dst = sbase + L::kKV + ring.stage * L::kSlotBytes;
+          if (has_v) {
+            const int sv = p.kv_begin + g * kBlockN;
+            tma_load_4d(dst, &tm_v, fb, 0, tc.h, sv, tc.b, pol_kv);
+            tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, tc.h, sv, tc.b, pol_kv);
+          }
+          if (has_k) {
+            const int sk0 = p.kv_begin + (g + 1) * kBlockN;
+            tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, tc.h, sk0, tc.b, pol_kv);
+            tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, tc.h, sk0, tc.b, pol_kv);
+          }
+          ring.advance<Slots>();
         }
       }
       if (!ok) {
@@ -306,7 +315,7 @@ __global__ void __launch_bounds__(384, 1)
         WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
         volatile uint32_t no_abort = 0;
         drain.abort = &no_abort;
-        for (int s = 0; s < Pairs; ++s)
+        for (int s = 0; s < Slots; ++s)
           if (armed_mask & (1u << s)) mbar_wait(bar(L::kKVFull + s), (armed_par >> s) & 1u, drain, kStatusTimeoutDrain);
       }
     }
@@ -331,9 +340,9 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t dv = make_sdesc_sw128(sbase, kBoxBytes, 1024);
       const uint32_t k_lo = static_cast<uint32_t>(dk), k_hi = static_cast<uint32_t>(dk >> 32);
       const uint32_t v_lo = static_cast<uint32_t>(dv), v_hi = static_cast<uint32_t>(dv >> 32);
-      auto issue_s = [&](int i, int slot) {
+      auto issue_s = [&](int i, int slot) {  // K of the group in `slot`
         const uint32_t qa = k_lo + ((L::kQ + i * kTileBytes) >> 4);
-        const uint32_t ka = k_lo + ((L::kKV + slot * L::kPairBytes) >> 4);
+        const uint32_t ka = k_lo + ((L::kKV + slot * L::kSlotBytes + kTileBytes) >> 4);
         const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int k = 0; k < kHeadDim / 16; ++k) {
@@ -342,8 +351,8 @@ __global__ void __launch_bounds__(384, 1)
         }
         tc_commit(bar(L::kSFull + i));
       };
-      auto issue_pv = [&](int i, int slot, bool acc) {
-        const uint32_t va = v_lo + ((L::kKV + slot * L::kPairBytes + kTileBytes) >> 4);
+      auto issue_pv = [&](int i, int slot, bool acc) {  // V of the group in `slot`
+        const uint32_t va = v_lo + ((L::kKV + slot * L::kSlotBytes) >> 4);
         const uint32_t d = tmem + 256 + i * 128;
         const uint32_t pa = tmem + i * 128;
         umma_ts_w(d, pa, va, v_hi, idesc_pv, acc ? 1u : 0u);
@@ -358,16 +367,18 @@ __global__ void __launch_bounds__(384, 1)
         if (N == 0) continue;
         if (!mbar_wait(bar(L::kQFull), q_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
         q_full_par ^= 1u;
+        // group G(-1) = {K0}
         if (!mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         if (n0 > 0) issue_s(0, ring.stage);
         if (n1 > 0) issue_s(1, ring.stage);
+        tc_commit(bar(L::kKVEmpty + ring.stage));
         if (N == 1) tc_commit(bar(L::kQEmpty));
+        ring.advance<Slots>();
         for (int j = 0; j < N && ok; ++j) {
+          // group G(j) = {V_j, K_j+1}
           const int cur = ring.stage;
-          Ring nxt = ring;
-          nxt.advance<Pairs>();
-          bool next_ready = false;
+          if (!mbar_wait(bar(L::kKVFull + cur), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
 #pragma unroll
           for (int i = 0; i < QTiles; ++i) {
             const int ni = i == 0 ? n0 : n1;
@@ -381,19 +392,12 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_after();
             issue_pv(i, cur, j > 0);
             if (j + 1 == ni) tc_commit(bar(L::kOFull + i));
-            if (j + 1 < ni) {
-              if (!next_ready) {
-                if (!mbar_wait(bar(L::kKVFull + nxt.stage), nxt.phase, ctl, kStatusTimeoutMma)) { ok = false; continue; }
-                next_ready = true;
-                tc_fence_after();
-              }
-              issue_s(i, nxt.stage);
-            }
+            if (j + 1 < ni) issue_s(i, cur);
           }
           if (!ok) break;
-          tc_commit(bar(L::kKVEmpty + cur));  // K(j) and V(j) are no longer read
+          tc_commit(bar(L::kKVEmpty + cur));  // V_j and K_j+1 are no longer read
           if (j + 2 == N) tc_commit(bar(L::kQEmpty));
-          ring = nxt;
+          ring.advance<Slots>();
         }
       }
       // Every MMA this thread issued has finished once this barrier flips.

@@ -79,19 +79,19 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 }
 
 // B200 tilings behind the reference's config ids (include/fav4_bshd.h:17-18):
-//   1: one 128-row Q tile per CTA, 3 K/V pair slots, MUFU exp2 only
-//   2: two 128-row Q tiles per CTA sharing each K/V pair (ping-pong),
-//      2 pair slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
+//   1: one 128-row Q tile per CTA, 3 K/V ring slots, MUFU exp2 only
+//   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
+//      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
-template <bool Causal, int QTiles, int Pairs, int PolyPer8>
+template <bool Causal, int QTiles, int Slots, int PolyPer8>
 int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   DeviceInfo info;
   if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
-  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Pairs, PolyPer8>;
-  constexpr int smem = SmemLayout<QTiles, Pairs>::kAlloc;
+  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8>;
+  constexpr int smem = SmemLayout<QTiles, Slots>::kAlloc;
   {
     static std::mutex mu;
     static bool attr_set[kMaxDevices] = {};
