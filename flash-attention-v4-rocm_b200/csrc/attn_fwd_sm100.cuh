@@ -231,9 +231,9 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(L::kSFull + i), 1);
-      mbar_init(bar(L::kPFull + i), 128);
+      mbar_init(bar(L::kPFull + i), 4);   // one arrival per softmax warp
       mbar_init(bar(L::kOFull + i), 1);
-      mbar_init(bar(L::kOEmpty + i), 128);
+      mbar_init(bar(L::kOEmpty + i), 4);
     }
     mbar_init(bar(L::kTeardown), 1);
     fence_mbar_init();
@@ -375,29 +375,40 @@ __global__ void __launch_bounds__(384, 1)
         tc_commit(bar(L::kKVEmpty + ring.stage));
         if (N == 1) tc_commit(bar(L::kQEmpty));
         ring.advance<Slots>();
+        // G(0) is awaited while the S MMAs above drain.
+        if (!mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
         for (int j = 0; j < N && ok; ++j) {
-          // group G(j) = {V_j, K_j+1}
+          // group G(j) = {V_j, K_j+1} is resident (awaited one step earlier).
+          // Between the last MMA of one batch and the first of the next only
+          // a commit, a P wait and a fence remain: everything else sits in the
+          // shadow of MMAs the tensor pipe is still working through.
           const int cur = ring.stage;
-          if (!mbar_wait(bar(L::kKVFull + cur), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+          Ring nxt = ring;
+          nxt.advance<Slots>();
 #pragma unroll
           for (int i = 0; i < QTiles; ++i) {
             const int ni = i == 0 ? n0 : n1;
-            if (j >= ni || !ok) continue;
-            if (!mbar_wait(bar(L::kPFull + i), p_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
-            p_par[i] ^= 1u;
-            if (j == 0) {
-              if (!mbar_wait(bar(L::kOEmpty + i), o_empty_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
-              o_empty_par[i] ^= 1u;
+            if (j < ni && ok) {
+              if (!mbar_wait(bar(L::kPFull + i), p_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
+              p_par[i] ^= 1u;
+              if (j == 0) {
+                if (!mbar_wait(bar(L::kOEmpty + i), o_empty_par[i], ctl, kStatusTimeoutMma)) { ok = false; continue; }
+                o_empty_par[i] ^= 1u;
+              }
+              tc_fence_after();
+              issue_pv(i, cur, j > 0);
+              if (j + 1 == ni) tc_commit(bar(L::kOFull + i));
             }
-            tc_fence_after();
-            issue_pv(i, cur, j > 0);
-            if (j + 1 == ni) tc_commit(bar(L::kOFull + i));
-            if (j + 1 < ni) issue_s(i, cur);
+            if (i == QTiles - 1 && j + 1 < N && ok) {
+              // next group, awaited behind this tile's PV MMAs
+              if (!mbar_wait(bar(L::kKVFull + nxt.stage), nxt.phase, ctl, kStatusTimeoutMma)) { ok = false; continue; }
+            }
+            if (j + 1 < ni && ok) issue_s(i, cur);
           }
           if (!ok) break;
           tc_commit(bar(L::kKVEmpty + cur));  // V_j and K_j+1 are no longer read
           if (j + 2 == N) tc_commit(bar(L::kQEmpty));
-          ring.advance<Slots>();
+          ring = nxt;
         }
       }
       // Every MMA this thread issued has finished once this barrier flips.
@@ -493,7 +504,8 @@ __global__ void __launch_bounds__(384, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(L::kPFull + i));
+        __syncwarp();  // every lane's P / O stores are complete
+        if (lane == 0) mbar_arrive(bar(L::kPFull + i));
       }
       if (!ok) break;
       // ------------------------------ epilogue ------------------------------
@@ -524,7 +536,8 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(bar(L::kOEmpty + i));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
       } else if (live) {
         uint4* dst = reinterpret_cast<uint4*>(orow_ptr);
 #pragma unroll
