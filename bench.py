@@ -223,6 +223,42 @@ def run_reference_arm(args, rank, world):
           "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
+def run_sweep(args):
+    """B32 H8 D128, S in {512..32768}, dense and causal,
+    one GPU. For each point: W untimed calls, then K calls timed with CUDA
+    events; prints one JSON line per point (the driver's bench line is the
+    default mode, not this one)."""
+    import torch
+
+    import fav4_bshd
+    runner = fav4_bshd.Runner()
+    pk, pk_kind = peaks()
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    for n in [int(x) for x in args.seqs.split(",")]:
+        q, k, v = (torch.randn((B, n, H, D), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+        o = torch.empty_like(q)
+        for causal in (False, True):
+            for _ in range(max(3, args.warmup)):
+                runner.call(q, k, v, o, None, causal, args.config)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                runner.call(q, k, v, o, None, causal, args.config)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / args.steps
+            f = flops(B, H, n, causal)
+            tf = f / us / 1e6
+            byts = 4 * B * n * H * D * 2
+            emit({"seq": n, "causal": causal, "us": us, "tflops": tf, "frac_of_measured_bf16": tf / pk["bf16_tflops"],
+                  "frac_of_nominal_2250": tf / 2250.0, "gbs": byts / us / 1e3,
+                  "frac_of_measured_hbm": byts / us / 1e3 / pk["hbm_gbs"], "peak_source": pk_kind,
+                  "batch": B, "heads": H, "config": args.config})
+        del q, k, v, o
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -234,7 +270,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=B, help="profiling only: per-GPU batch")
     ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
+    ap.add_argument("--sweep", action="store_true", help="BASELINE configs[2] sequence sweep, one GPU")
+    ap.add_argument("--seqs", default="512,1024,2048,4096,8192,16384,32768")
     args = ap.parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     if (args.batch, args.seq) != (B, S):
         set_shape(args.batch, args.seq)
     args.warmup = max(3, args.warmup)
