@@ -17,6 +17,9 @@ Contents, each restating the reference (rocking5566/flash-attention-v4-rocm):
   device='cuda' and scale=1/sqrt(128); here scale is a parameter).
 * ``errors``: the reference's BF16 acceptance test (benchmarks/bshd.py:22-32)
   plus the north-star bounds max|dO| <= 2e-2, mean|dO| <= 2e-3, |dLSE| <= 1e-3.
+* ``combine``: the LSE-weighted merge of split-KV partials that the library's
+  combine kernel computes (the reference has no split-KV path; this is the
+  checker for it).
 * ``emulate``: a kernel-faithful FP32 emulation (tiles of 128 keys, lazy
   rescale with threshold 8 base-2 units, P rounded to BF16, row sum over the
   unrounded FP32 probabilities: src/bshd_kernel.hpp:148-181) that explains the
@@ -291,3 +294,20 @@ def emulate(q, k, v, causal: bool, scale: float | None = None, block_n: int = 12
             o_out[bi, :, hi] = bf16_round(acc * inv[:, None])
             lse_out[bi, hi] = lse
     return o_out, lse_out
+
+
+def combine(o_parts, lse_parts):
+    """Merge split-KV partials: LSE = log(sum_g exp(LSE_g)), O = sum_g
+    exp(LSE_g - LSE) O_g. o_parts[g] [B,S,H,128], lse_parts[g] [B,H,S]; rows
+    whose every part is empty (-inf) get O = 0 and LSE = -inf."""
+    lses = np.stack([np.asarray(x, np.float64) for x in lse_parts])  # [G,B,H,S]
+    mx = lses.max(0)
+    safe = np.where(np.isneginf(mx), 0.0, mx)
+    w = np.where(np.isneginf(lses), 0.0, np.exp(lses - safe))
+    wsum = w.sum(0)
+    o = sum(w[g].transpose(0, 2, 1)[..., None] * np.asarray(o_parts[g], np.float64) for g in range(len(o_parts)))
+    ws = wsum.transpose(0, 2, 1)[..., None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        o = np.where(ws > 0, o / np.where(ws > 0, ws, 1.0), 0.0)
+        lse = np.where(wsum > 0, safe + np.log(np.where(wsum > 0, wsum, 1.0)), -np.inf)
+    return o, lse
