@@ -259,6 +259,65 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def run_long_context(args, rank, world, local):
+    """B1 H8 S131072 causal, KV split over the N ranks of
+    this torchrun job (fav4_bshd.splitkv: zigzag chunks, combine over NVLink
+    peer reads). Times K forward steps (device events, max over ranks), then
+    checks every rank's output rows against a single-GPU forward of the whole
+    problem on that rank. One JSON line from rank 0."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import fav4_bshd
+    from fav4_bshd.splitkv import SplitKV
+    for key, val in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29531"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+        os.environ.setdefault(key, val)  # single process without torchrun
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        b, h, n = 1, 8, args.lc_seq
+        gen = torch.Generator(device=dev).manual_seed(4)  # same inputs on every rank
+        q, k, v = (torch.randn((b, n, h, D), generator=gen, device=dev, dtype=torch.bfloat16) for _ in range(3))
+        sk = SplitKV(dist.group.WORLD, b, h, n, n, dev)
+        for _ in range(max(1, args.warmup)):
+            sk.forward(q, k, v, True, args.config)
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            o, lse = sk.forward(q, k, v, True, args.config)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        # agreement with one GPU computing the whole problem
+        full_o = torch.empty_like(q)
+        full_l = torch.empty((b, h, n), device=dev, dtype=torch.float32)
+        fav4_bshd.Runner().call(q, k, v, full_o, full_l, True, args.config)
+        torch.cuda.synchronize()
+        err = torch.tensor([(o.float() - full_o[:, sk.r0:sk.r1].float()).abs().max().item(),
+                            (o.float() - full_o[:, sk.r0:sk.r1].float()).abs().mean().item(),
+                            (lse - full_l[:, :, sk.r0:sk.r1]).abs().max().item()], device=dev, dtype=torch.float64)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        f = flops(b, h, n, True)
+        if rank == 0:
+            emit({"mode": "long_context_split_kv", "metric": "causal fwd TFLOPS, B1 H8 D128, KV split over GPUs",
+                  "value": f / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                  "ms_per_step": ms, "seq_len": n, "heads": h, "config": args.config,
+                  "vs_single_gpu": {"max_abs_o": err[0].item(), "mean_abs_o": err[1].item(),
+                                    "max_abs_lse": err[2].item(),
+                                    "within_tolerance": bool(err[0] <= 2e-2 and err[1] <= 2e-3 and err[2] <= 1e-3)}})
+        del sk
+    finally:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -272,6 +331,9 @@ def main():
     ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
     ap.add_argument("--sweep", action="store_true", help="BASELINE configs[2] sequence sweep, one GPU")
     ap.add_argument("--seqs", default="512,1024,2048,4096,8192,16384,32768")
+    ap.add_argument("--long-context", action="store_true",
+                    help="BASELINE configs[4]: B1 H8 causal split-KV across the torchrun ranks")
+    ap.add_argument("--lc-seq", type=int, default=131072)
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
@@ -283,6 +345,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.long_context:
+        run_long_context(args, rank, world, local)
+        return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
