@@ -261,6 +261,152 @@ extern "C" int fav4_bshd_forward_splitkv_static(const Fav4Args* a, int causal, i
   return fav4_bshd_combine(o_parts, lse_parts, parts, a->o, a->lse, a->batch, a->heads, a->sq, stream);
 }
 
+// --------------------------------------------------------------------------
+// Forward from host buffers, pipelined over batch chunks: the copy of chunk
+// c+1 to the device, the forwards of chunk c and the copy of chunk c-1 back
+// to the host run at the same time (two copy streams beside the caller's
+// stream; PCIe copies in both directions overlap each other and the kernels).
+namespace fav4 {
+namespace {
+
+constexpr int kMaxHostOuts = 8;
+
+struct HostLayout {
+  int chunk_batch = 0, chunks = 0, slots = 0;
+  size_t q = 0, kv = 0, o = 0, lse = 0;  // bytes of one chunk's tensors (rounded to 256)
+  size_t slot = 0;                       // bytes of one staging slot
+};
+
+bool host_layout(const Fav4Args* a, const Fav4HostOut* outs, int n_outs, int chunks, HostLayout* l) {
+  if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->sk <= 0 || n_outs < 1 || n_outs > kMaxHostOuts ||
+      chunks < 1 || a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128) ||
+      a->sk > INT_MAX / (a->heads * 128))
+    return false;
+  l->chunks = chunks < a->batch ? chunks : a->batch;
+  l->chunk_batch = (a->batch + l->chunks - 1) / l->chunks;
+  l->chunks = (a->batch + l->chunk_batch - 1) / l->chunk_batch;
+  l->slots = l->chunks > 1 ? 2 : 1;
+  const size_t row = static_cast<size_t>(a->heads) * kHeadDim * 2;
+  l->q = round256(static_cast<size_t>(l->chunk_batch) * a->sq * row);
+  l->kv = round256(static_cast<size_t>(l->chunk_batch) * a->sk * row);
+  l->o = l->q;
+  l->lse = round256(static_cast<size_t>(l->chunk_batch) * a->heads * a->sq * 4);
+  l->slot = l->q + 2 * l->kv;
+  for (int j = 0; j < n_outs; ++j) l->slot += l->o + ((outs && outs[j].lse) ? l->lse : 0);
+  return true;
+}
+
+// Streams and events of one call, released when the call returns (the
+// runtime frees them once the work queued on them has finished).
+struct HostPipe {
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t fork = nullptr, uploaded[2] = {}, computed[2] = {}, downloaded[2] = {};
+  cudaError_t create() {
+    cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
+    cudaEvent_t* all[] = {&fork, &uploaded[0], &uploaded[1], &computed[0], &computed[1], &downloaded[0],
+                          &downloaded[1]};
+    for (cudaEvent_t* ev : all)
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    return e;
+  }
+  ~HostPipe() {
+    cudaEvent_t all[] = {fork, uploaded[0], uploaded[1], computed[0], computed[1], downloaded[0], downloaded[1]};
+    for (cudaEvent_t ev : all)
+      if (ev) cudaEventDestroy(ev);
+    if (up) cudaStreamDestroy(up);
+    if (down) cudaStreamDestroy(down);
+  }
+};
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" size_t fav4_bshd_host_workspace_bytes(const Fav4Args* a, const Fav4HostOut* outs, int n_outs,
+                                                  int chunks) {
+  fav4::HostLayout l;
+  if (!outs || !fav4::host_layout(a, outs, n_outs, chunks, &l)) return 0;
+  return static_cast<size_t>(l.slots) * l.slot;
+}
+
+extern "C" int fav4_bshd_forward_host(const Fav4Args* a, const Fav4HostOut* outs, int n_outs, int chunks,
+                                      void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  fav4::HostLayout l;
+  if (!outs || !fav4::host_layout(a, outs, n_outs, chunks, &l) || !a->q || !a->k || !a->v ||
+      !std::isfinite(a->scale) || a->scale <= 0 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < static_cast<size_t>(l.slots) * l.slot)
+    return cudaErrorInvalidValue;
+  for (int j = 0; j < n_outs; ++j)
+    if (!outs[j].o || (outs[j].causal != 0 && outs[j].causal != 1) || outs[j].config < 0 || outs[j].config > 3)
+      return cudaErrorInvalidValue;
+  fav4::HostPipe pipe;
+  cudaError_t e = pipe.create();
+  if (e != cudaSuccess) return e;
+  // The copy streams start behind everything already queued on the caller's stream.
+  e = cudaEventRecord(pipe.fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pipe.up, pipe.fork, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pipe.down, pipe.fork, 0);
+  if (e != cudaSuccess) return e;
+  const size_t row = static_cast<size_t>(a->heads) * fav4::kHeadDim * 2;  // bytes of one (token) row
+  const size_t lse_row = static_cast<size_t>(a->heads) * a->sq * 4;        // LSE bytes of one batch entry
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  int last = 0;
+  for (int c = 0; c < l.chunks && e == cudaSuccess; ++c) {
+    const int s = c % l.slots;
+    last = s;
+    const int b0 = c * l.chunk_batch;
+    const int nb = b0 + l.chunk_batch <= a->batch ? l.chunk_batch : a->batch - b0;
+    unsigned char* slot = ws + s * l.slot;
+    unsigned char *dq = slot, *dk = slot + l.q, *dv = slot + l.q + l.kv;
+    const size_t q_bytes = static_cast<size_t>(nb) * a->sq * row, kv_bytes = static_cast<size_t>(nb) * a->sk * row;
+    // upload: the slot's inputs are free once the forwards of chunk c-2 ran
+    if (c >= l.slots) e = cudaStreamWaitEvent(pipe.up, pipe.computed[s], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dq, static_cast<const unsigned char*>(a->q) + static_cast<size_t>(b0) * a->sq * row, q_bytes,
+                          cudaMemcpyHostToDevice, pipe.up);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dk, static_cast<const unsigned char*>(a->k) + static_cast<size_t>(b0) * a->sk * row, kv_bytes,
+                          cudaMemcpyHostToDevice, pipe.up);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dv, static_cast<const unsigned char*>(a->v) + static_cast<size_t>(b0) * a->sk * row, kv_bytes,
+                          cudaMemcpyHostToDevice, pipe.up);
+    if (e == cudaSuccess) e = cudaEventRecord(pipe.uploaded[s], pipe.up);
+    // forwards on the caller's stream, once the slot's outputs were copied out
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, pipe.uploaded[s], 0);
+    if (e == cudaSuccess && c >= l.slots) e = cudaStreamWaitEvent(stream, pipe.downloaded[s], 0);
+    unsigned char* out = slot + l.q + 2 * l.kv;
+    unsigned char* dst[fav4::kMaxHostOuts];
+    float* dst_lse[fav4::kMaxHostOuts];
+    for (int j = 0; j < n_outs && e == cudaSuccess; ++j) {
+      Fav4Args ca = *a;
+      ca.q = dq;
+      ca.k = dk;
+      ca.v = dv;
+      ca.batch = nb;
+      ca.o = dst[j] = out;
+      out += l.o;
+      ca.lse = dst_lse[j] = outs[j].lse ? reinterpret_cast<float*>(out) : nullptr;
+      if (outs[j].lse) out += l.lse;
+      e = static_cast<cudaError_t>(fav4_bshd_forward(&ca, outs[j].causal, outs[j].config, stream));
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(pipe.computed[s], stream);
+    // download
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(pipe.down, pipe.computed[s], 0);
+    for (int j = 0; j < n_outs && e == cudaSuccess; ++j) {
+      e = cudaMemcpyAsync(static_cast<unsigned char*>(outs[j].o) + static_cast<size_t>(b0) * a->sq * row, dst[j], q_bytes,
+                          cudaMemcpyDeviceToHost, pipe.down);
+      if (e == cudaSuccess && outs[j].lse)
+        e = cudaMemcpyAsync(reinterpret_cast<unsigned char*>(outs[j].lse) + static_cast<size_t>(b0) * lse_row, dst_lse[j], static_cast<size_t>(nb) * lse_row,
+                            cudaMemcpyDeviceToHost, pipe.down);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(pipe.downloaded[s], pipe.down);
+  }
+  // Join: the caller's stream continues after the last copy back (copies on
+  // one stream complete in order, so the last one covers the others).
+  const cudaError_t j = cudaStreamWaitEvent(stream, pipe.downloaded[last], 0);
+  return e != cudaSuccess ? e : j;
+}
+
 extern "C" int fav4_bshd_pipeline_status(int clear) {
   uint32_t v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;

@@ -28,6 +28,12 @@ class Args(C.Structure):
         (n, C.c_int) for n in ("batch", "heads", "sq", "sk")] + [("scale", C.c_float)]
 
 
+class HostOut(C.Structure):
+    """Fav4HostOut (include/fav4_bshd.h): one output of fav4_bshd_forward_host."""
+
+    _fields_ = [("o", C.c_void_p), ("lse", C.c_void_p), ("causal", C.c_int), ("config", C.c_int)]
+
+
 _LIB = None
 _PROBE = None
 
@@ -44,6 +50,11 @@ def _bind(lib):
     lib.fav4_bshd_combine.restype = C.c_int
     lib.fav4_bshd_forward_splitkv_static.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_splitkv_static.restype = C.c_int
+    lib.fav4_bshd_host_workspace_bytes.argtypes = [C.POINTER(Args), C.POINTER(HostOut), C.c_int, C.c_int]
+    lib.fav4_bshd_host_workspace_bytes.restype = C.c_size_t
+    lib.fav4_bshd_forward_host.argtypes = [C.POINTER(Args), C.POINTER(HostOut), C.c_int, C.c_int, C.c_void_p,
+                                           C.c_size_t, C.c_void_p]
+    lib.fav4_bshd_forward_host.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
     lib.fav4_bshd_pipeline_status.restype = C.c_int
     return lib
@@ -142,6 +153,39 @@ class Runner:
         if status:
             raise RuntimeError(f"combine of {n} parts: CUDA status {status}")
 
+    def forward_host(self, q, k, v, outs, chunks=8, scale=None, stream=None, workspace=None):
+        """Forwards of host-resident (page-locked) Q/K/V through
+        fav4_bshd_forward_host: one upload, one output per (o, lse, causal,
+        config) in `outs` (o, lse: host tensors; lse may be None), copies and
+        kernels overlapped over `chunks` batch pieces. Ordered on `stream`;
+        the host outputs are complete once that stream is synchronised. The
+        device workspace is allocated with torch (and kept for the next call
+        of the same shape) unless one is given."""
+        import torch
+        assert all(x.dtype == torch.bfloat16 and not x.is_cuda and x.is_contiguous() for x in (q, k, v))
+        b, sq, h, d = q.shape
+        assert d == HEAD_DIM and k.shape == v.shape and k.shape[0] == b and k.shape[2:] == (h, d)
+        ho = (HostOut * len(outs))()
+        for j, (o, lse, causal, config) in enumerate(outs):
+            assert o.shape == q.shape and o.dtype == torch.bfloat16 and not o.is_cuda and o.is_contiguous()
+            assert lse is None or (lse.shape == (b, h, sq) and lse.dtype == torch.float32 and not lse.is_cuda)
+            ho[j] = HostOut(o.data_ptr(), _ptr(lse), int(causal), int(config))
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        a = Args(q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None, b, h, sq, k.shape[1], scale)
+        need = self.lib.fav4_bshd_host_workspace_bytes(C.byref(a), ho, len(outs), chunks)
+        if need == 0:
+            raise RuntimeError("forward_host: invalid arguments")
+        if workspace is None:
+            ws = getattr(self, "_host_ws", None)
+            if ws is None or ws.numel() < need or ws.device != torch.device("cuda", torch.cuda.current_device()):
+                ws = self._host_ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+            workspace = ws
+        assert workspace.is_cuda and workspace.numel() >= need
+        status = self.lib.fav4_bshd_forward_host(C.byref(a), ho, len(outs), chunks, workspace.data_ptr(),
+                                                 workspace.numel(), _stream(stream))
+        if status:
+            raise RuntimeError(f"forward_host: CUDA status {status}")
+
     def select_config(self, q, k, v, o, lse=None):
         a = self.args(q, k, v, o, lse)
         return self.lib.fav4_bshd_select_config(C.byref(a))
@@ -160,5 +204,5 @@ def forward(q, k, v, causal=False, config=0, scale=None, return_lse=False, out=N
     return (o, lse) if return_lse else o
 
 
-__all__ = ["Args", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
+__all__ = ["Args", "HostOut", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
            "HEAD_DIM", "CUDA_ERROR_INVALID_VALUE"]

@@ -88,6 +88,38 @@ int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts,
 int fav4_bshd_forward_splitkv_static(const Fav4Args* args, int causal, int config, int splits,
                                      cudaStream_t stream);
 
+/* One output of fav4_bshd_forward_host: host buffers for O (BF16
+ * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and
+ * the mask and config it is computed with. */
+struct Fav4HostOut {
+  void* o;
+  float* lse;
+  int causal;
+  int config;
+};
+typedef struct Fav4HostOut Fav4HostOut;
+
+/* Device workspace fav4_bshd_forward_host needs for these arguments, in
+ * bytes (0 when the arguments are invalid). */
+size_t fav4_bshd_host_workspace_bytes(const Fav4Args* args, const Fav4HostOut* outs, int n_outs, int chunks);
+
+/* Forward from host memory (no reference counterpart: the reference's caller
+ * copies to the device itself). args->q/k/v are HOST pointers (page-locked
+ * memory is needed for the copies to overlap); args->o and args->lse are
+ * ignored. Every output in outs[0..n_outs) (1..8 of them, e.g. a dense and a
+ * causal forward of the same inputs) is computed from one upload. The batch
+ * is cut into `chunks` pieces staged through two slots of `workspace`
+ * (device memory, 256-byte aligned, fav4_bshd_host_workspace_bytes long):
+ * the upload of one piece, the forwards of the previous one and the download
+ * of the one before that overlap. Work is ordered after what is already on
+ * `stream`, and `stream` waits for the last download, so a synchronise of
+ * `stream` (or an event recorded on it) means the host outputs are written.
+ * Results are bit-identical to fav4_bshd_forward on device copies. Calls that
+ * share a workspace must not overlap. Returns 0, cudaErrorInvalidValue, or
+ * the first failing CUDA status. */
+int fav4_bshd_forward_host(const Fav4Args* args, const Fav4HostOut* outs, int n_outs, int chunks, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream);
+
 /* Failure detection (no reference counterpart): every pipeline wait inside the
  * kernels is bounded in time (default 2000 ms, environment variable
  * FAV4_WAIT_LIMIT_MS). A wait that runs out makes the kernel stop cleanly and

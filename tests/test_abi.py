@@ -22,7 +22,7 @@ def declared_functions():
     names = []
     for h in HEADERS:
         text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        names += re.findall(r"^\s*int\s+(fav4_\w+)\s*\(", text, flags=re.M)
+        names += re.findall(r"^\s*(?:int|size_t)\s+(fav4_\w+)\s*\(", text, flags=re.M)
     return names
 
 
@@ -129,3 +129,49 @@ def test_combine_rejects_invalid_arguments(lib):
     assert f(o, lse, 2, A16 * 5, None, 0, 8, 64, None) == INVALID        # empty batch
     bad = (C.c_void_p * 2)(A16, None)
     assert f(bad, lse, 2, A16 * 5, None, 1, 8, 64, None) == INVALID      # null part
+
+
+def _host_case(n_outs=2, lse=(True, False), **kw):
+    a = make_args(o=None, **kw)
+    outs = (F.HostOut * max(n_outs, 1))()
+    for j in range(n_outs):
+        outs[j] = F.HostOut(A16 * (6 + j), A16 * 9 if lse[j % len(lse)] else None, j % 2, 0)
+    return a, outs
+
+
+def test_host_workspace_bytes_formula(lib):
+    # B=5 cut into 3 chunks -> pieces of 2, 2, 1 batch entries, two staging slots
+    a, outs = _host_case(batch=5, heads=8, sq=64, sk=96)
+    r256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    q = r256(2 * 64 * 8 * 256)
+    kv = r256(2 * 96 * 8 * 256)
+    lse = r256(2 * 8 * 64 * 4)
+    slot = q + 2 * kv + 2 * q + lse  # two outputs, only the first with LSE
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 2, 3) == 2 * slot
+    # one chunk -> one slot; more chunks than batch entries -> one entry each
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 2, 1) == \
+        r256(5 * 64 * 8 * 256) * 3 + 2 * r256(5 * 96 * 8 * 256) + r256(5 * 8 * 64 * 4)
+    one = r256(64 * 8 * 256) * 3 + 2 * r256(96 * 8 * 256) + r256(8 * 64 * 4)
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 2, 99) == 2 * one
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 0, 3) == 0
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 9, 3) == 0
+    assert lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 2, 0) == 0
+
+
+def test_host_forward_rejects_invalid_arguments(lib):
+    a, outs = _host_case()
+    need = lib.fav4_bshd_host_workspace_bytes(C.byref(a), outs, 2, 2)
+    f = lib.fav4_bshd_forward_host
+    ws = A16 * 16
+    assert f(C.byref(a), outs, 2, 2, ws, need - 1, None) == INVALID      # workspace too small
+    assert f(C.byref(a), outs, 2, 2, ws + 128, need, None) == INVALID    # misaligned workspace
+    assert f(C.byref(a), outs, 2, 2, None, need, None) == INVALID        # no workspace
+    assert f(C.byref(a), None, 2, 2, ws, need, None) == INVALID          # no outputs
+    assert f(C.byref(a), outs, 0, 2, ws, need, None) == INVALID
+    for kw in (dict(q=None), dict(k=None), dict(v=None), dict(scale=0.0), dict(sq=0), dict(batch=0)):
+        b, o2 = _host_case(**kw)
+        assert f(C.byref(b), o2, 2, 2, ws, need, None) == INVALID, kw
+    bad = [F.HostOut(None, None, 0, 0), F.HostOut(A16, None, 2, 0), F.HostOut(A16, None, 0, 4)]
+    for h in bad:
+        o1 = (F.HostOut * 1)(h)
+        assert f(C.byref(a), o1, 1, 2, ws, need, None) == INVALID
