@@ -261,6 +261,95 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def _library_impls(torch):
+    """Same-box attention libraries on identical BSHD tensors (the analogue of
+    the reference's CK comparator, benchmarks/ck_bshd.hip:62-66): each entry
+    maps (q, k, v, causal, scale) -> O in BSHD, or is the reason it cannot run."""
+    import torch.nn.functional as Fn
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    def sdpa(backend):
+        def run(q, k, v, causal, scale):
+            with sdpa_kernel(backend):
+                o = Fn.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                    is_causal=causal, scale=scale)
+            return o.transpose(1, 2)
+        return run
+
+    impls = {"torch-sdpa-cudnn": sdpa(SDPBackend.CUDNN_ATTENTION),
+             "torch-sdpa-flash": sdpa(SDPBackend.FLASH_ATTENTION)}
+    try:
+        from flash_attn import __version__ as fa_version
+        from flash_attn import flash_attn_func
+
+        impls[f"flash_attn-{fa_version}"] = lambda q, k, v, causal, scale: flash_attn_func(
+            q, k, v, causal=causal, softmax_scale=scale)
+    except Exception as e:  # noqa: BLE001
+        impls["flash_attn"] = f"import failed: {type(e).__name__}: {e}"
+    return impls
+
+
+def run_compare(args):
+    """Same-box comparison (one GPU): this library and the installed attention
+    libraries on the same Q/K/V (B32 H8 D128 BF16, seed 2), dense and causal,
+    for each sequence length of --seqs. Calls of all implementations are
+    interleaved over --steps rounds; one JSON line per (seq, mask,
+    implementation) with the median time and the max |dO| against this
+    library's output."""
+    import torch
+
+    import fav4_bshd
+    runner = fav4_bshd.Runner()
+    impls = _library_impls(torch)
+    scale = 1 / math.sqrt(D)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    for n in [int(x) for x in args.seqs.split(",")]:
+        q, k, v = (torch.randn((B, n, H, D), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+        o = torch.empty_like(q)
+        for causal in (False, True):
+            def ours():
+                runner.call(q, k, v, o, None, causal, args.config)
+                return o
+            runs = {"fav4_bshd (this library)": ours}
+            notes = {}
+            for name, fn in impls.items():
+                if isinstance(fn, str):
+                    notes[name] = fn
+                    continue
+                try:
+                    fn(q, k, v, causal, scale)
+                    torch.cuda.synchronize()
+                    runs[name] = (lambda fn=fn: fn(q, k, v, causal, scale))
+                except Exception as e:  # noqa: BLE001
+                    notes[name] = f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"
+                    torch.cuda.synchronize()
+            ref = ours().clone()
+            diffs = {name: float((fn().float() - ref.float()).abs().max()) for name, fn in runs.items()}
+            times = {name: [] for name in runs}
+            for _ in range(max(3, args.warmup)):
+                for fn in runs.values():
+                    fn()
+            torch.cuda.synchronize()
+            for _ in range(args.steps):
+                for name, fn in runs.items():
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn()
+                    e1.record()
+                    e1.synchronize()
+                    times[name].append(e0.elapsed_time(e1) * 1e3)
+            f = flops(B, H, n, causal)
+            for name in runs:
+                us = statistics.median(times[name])
+                emit({"mode": "compare", "impl": name, "seq": n, "causal": causal, "us": us, "tflops": f / us / 1e6,
+                      "max_abs_diff_vs_fav4": diffs[name], "batch": B, "heads": H, "head_dim": D,
+                      "timing": f"median of {args.steps} single calls, CUDA events, calls interleaved"})
+            for name, why in notes.items():
+                emit({"mode": "compare", "impl": name, "seq": n, "causal": causal, "unavailable": why})
+        del q, k, v, o
+        torch.cuda.empty_cache()
+
+
 def run_long_context(args, rank, world, local):
     """B1 H8 S131072 causal, KV split over the N ranks of
     this torchrun job (fav4_bshd.splitkv: zigzag chunks, combine over NVLink
@@ -332,6 +421,8 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="profiling only: per-GPU batch")
     ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
     ap.add_argument("--sweep", action="store_true", help="BASELINE configs[2] sequence sweep, one GPU")
+    ap.add_argument("--compare", action="store_true",
+                    help="same-box comparison with torch SDPA (cuDNN, flash) and flash_attn, one GPU")
     ap.add_argument("--seqs", default="512,1024,2048,4096,8192,16384,32768")
     ap.add_argument("--long-context", action="store_true",
                     help="BASELINE configs[4]: B1 H8 causal split-KV across the torchrun ranks")
@@ -340,6 +431,9 @@ def main():
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
+        return
+    if args.compare:
+        run_compare(args)
         return
     if (args.batch, args.seq) != (B, S):
         set_shape(args.batch, args.seq)
