@@ -11,7 +11,11 @@
 //                      query row) per thread; exp2 online softmax with the lazy
 //                      rescale of bshd_kernel.hpp:155-164 (threshold 8 base-2
 //                      units); the rare O correction is done in TMEM by the row
-//                      owner; epilogue O/l -> BF16 and LSE (bshd_kernel.hpp:195-210).
+//                      owner; epilogue O/l -> BF16 and LSE (bshd_kernel.hpp:195-210):
+//                      each 64-column half of the O tile goes through a 16 KiB
+//                      shared-memory stage and one TMA store (whole 128-byte row
+//                      pieces instead of 16-byte stores to 32 rows per
+//                      instruction; rows past Sq are clipped by the store).
 //
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_i (BF16 pairs, 64 columns) overwrites the first half of S_i.
@@ -101,7 +105,8 @@ struct SmemLayout {
   static constexpr int kTeardown = kNumBars - 1;
   static constexpr int kTmemHolder = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemHolder + 4;
-  static constexpr int kBytes = kAbort + 4;
+  static constexpr int kStage = (kAbort + 4 + 1023) & ~1023;  // [Q tile] O store stage: 128 rows x 128 B
+  static constexpr int kBytes = kStage + QTiles * kBoxBytes;
   static constexpr int kAlloc = kBytes + 1024;                // slack for 1 KiB alignment
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
@@ -207,7 +212,8 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 template <bool Causal, int QTiles, int Slots, int PolyPer8>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                          const FwdParams p) {
   using L = SmemLayout<QTiles, Slots>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -242,6 +248,7 @@ __global__ void __launch_bounds__(384, 1)
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
   }
   if (warp == 9) {
     tmem_alloc(smem_addr(tmem_holder), 512);
@@ -428,6 +435,10 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
     const uint32_t t_s = tmem + lane_off + i * 128;
     const uint32_t t_o = tmem + lane_off + 256 + i * 128;
+    // O store stage of this Q tile: 16-byte chunk c of a row at (c ^ (row % 8)), the TMA 128-byte swizzle
+    uint8_t* stage_row = smem + L::kStage + i * kBoxBytes + row * 128;
+    const uint32_t stage = sbase + L::kStage + i * kBoxBytes;
+    const bool issuer = warp % 4 == 0 && lane == 0;  // issues this warpgroup's O stores
     uint32_t s_par = 0, o_full_par = 0;
     const float scale_log2 = p.scale_log2;
     bool ok = true;
@@ -507,47 +518,62 @@ __global__ void __launch_bounds__(384, 1)
         __syncwarp();  // every lane's P / O stores are complete
         if (lane == 0) mbar_arrive(bar(L::kPFull + i));
       }
-      if (!ok) break;
       // ------------------------------ epilogue ------------------------------
       const bool live = grow < p.sq;
-      __nv_bfloat16* orow_ptr =
-          p.o + ((static_cast<int64_t>(tc.b) * p.sq + grow) * p.heads + tc.h) * kHeadDim;
       if (ni > 0) {
-        if (!warp_wait(bar(L::kOFull + i), o_full_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+        // The four warps of this warpgroup meet at 128-thread AND-barriers
+        // (id 1 + i); a warp that gave up on a wait above arrives with
+        // `false`, so all four leave together.
+        const bool got = ok && warp_wait(bar(L::kOFull + i), o_full_par, ctl, kStatusTimeoutSoftmax);
+        if (issuer) tma_store_wait_read_all();  // the previous tile's stores have read the stage
+        if (!pair_all(1 + i, 128, got)) { ok = false; break; }
         o_full_par ^= 1u;
         tc_fence_after();
         const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t orow[32];
-          tmem_ld32(t_o + c * 32, orow);
-          tmem_ld_wait();
-          if (live) {
-            uint4* dst = reinterpret_cast<uint4*>(orow_ptr + c * 32);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
-              dst[v] = w;
-            }
+          for (int c = 0; c < 2; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(t_o + half * 64 + c * 32, orow);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[c * 16 + e] = pack_bf16x2(__uint_as_float(orow[2 * e]) * inv, __uint_as_float(orow[2 * e + 1]) * inv);
+          }
+          if (half == 1) {
+            tc_fence_before();
+            __syncwarp();  // every lane has read its row of O_i
+            if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
+            pair_all(1 + i, 128, true);  // the store of columns 0-63 has read the stage
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stage_row + ((c ^ (row & 7)) * 16)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
+          pair_all(1 + i, 128, true);  // every row of this half is staged
+          if (issuer) {
+            tma_store_4d(&tm_o, stage, half * 64, tc.h, r0, tc.b);
+            tma_store_commit();
+            if (half == 0) tma_store_wait_read_all();
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
       } else if (live) {
-        uint4* dst = reinterpret_cast<uint4*>(orow_ptr);
+        // no key visible to this Q tile (a split-KV slice): O = 0
+        uint4* dst = reinterpret_cast<uint4*>(p.o + ((static_cast<int64_t>(tc.b) * p.sq + grow) * p.heads + tc.h) *
+                                                        kHeadDim);
 #pragma unroll
         for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0u, 0u, 0u, 0u);
       }
+      if (!ok) break;
       if (live && p.lse != nullptr) {
         p.lse[(static_cast<int64_t>(tc.b) * p.heads + tc.h) * p.sq + grow] =
             l > 0.f ? m * kLn2 + logf(l) : -INFINITY;
       }
     }
+    if (issuer) tma_store_wait_all();  // every O store is complete before the CTA exits
   } else {
     regs_release<kOtherRegs>();  // warps 4-7 when QTiles == 1: Q tile 1 unused
   }

@@ -79,7 +79,7 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 }
 
 // B200 tilings behind the reference's config ids (include/fav4_bshd.h:17-18):
-//   1: one 128-row Q tile per CTA, 3 K/V ring slots, MUFU exp2 only
+//   1: one 128-row Q tile per CTA, 2 K/V ring slots, MUFU exp2 only
 //   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
@@ -102,9 +102,9 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
       attr_set[dev] = true;
     }
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, a.heads) ||
-      !encode_bshd(&tv, a.v, a.batch, a.sk, a.heads))
+      !encode_bshd(&tv, a.v, a.batch, a.sk, a.heads) || !encode_bshd(&to, a.o, a.batch, a.sq, a.heads))
     return cudaErrorInvalidValue;
   FwdParams p;
   p.o = static_cast<__nv_bfloat16*>(a.o);
@@ -123,14 +123,14 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
   p.status = info.status;
   p.wait_limit_ns = wait_limit_ns();
   const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
-  kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, p);
+  kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }
 
 template <bool Causal>
 int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream) {
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 3, 0>(a, kv_begin, kv_end, stream);
+    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_begin, kv_end, stream);
     case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_begin, kv_end, stream);
     case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_begin, kv_end, stream);
     default: return cudaErrorInvalidValue;
