@@ -1,0 +1,77 @@
+"""PyTorch operator for the attention forward: ``torch.ops.fav4.bshd_forward``.
+
+The reference's callers build the ``Fav4Args`` structure by hand for every
+call (benchmarks/bshd.py:64-74). This module registers the C ABI as a PyTorch
+custom operator instead, so a caller passes tensors and PyTorch handles the
+output allocation, the current stream and tracing:
+
+    o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, scale, return_lse)
+
+* q, k, v: CUDA BF16 ``[B, S, H, 128]``, contiguous (the reference contract,
+  include/fav4_bshd.h:12-15); k and v share their shape.
+* causal: top-left causal mask. config: 0 (Auto) to 3. scale: softmax scale,
+  or a non-positive value for 1/sqrt(128).
+* Returns O (BF16, q's shape) and LSE (FP32 ``[B, H, Sq]``, natural log), or
+  an empty LSE tensor when ``return_lse`` is False.
+
+The CUDA kernel runs through ``fav4_bshd_forward`` on the current stream, so
+the operator can be captured in a CUDA graph. A fake (meta) implementation
+gives shapes to FakeTensor tracing and ``torch.compile`` graphs, so the op
+composes with both. It has no autograd formula: the library implements the
+forward pass only, and asking for a gradient raises.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import HEAD_DIM, Runner
+
+_RUNNER: Runner | None = None
+
+
+def _runner() -> Runner:
+    global _RUNNER
+    if _RUNNER is None:
+        _RUNNER = Runner()
+    return _RUNNER
+
+
+def _check(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config: int) -> None:
+    torch._check(q.dim() == 4 and q.shape[-1] == HEAD_DIM, lambda: f"q must be [B, S, H, {HEAD_DIM}], got {q.shape}")
+    torch._check(k.shape == v.shape, lambda: f"k and v shapes differ: {k.shape} vs {v.shape}")
+    torch._check(k.dim() == 4 and k.shape[0] == q.shape[0] and k.shape[2:] == q.shape[2:],
+                 lambda: f"k must be [B, Sk, H, {HEAD_DIM}] with q's B and H, got {k.shape}")
+    torch._check(all(x.dtype == torch.bfloat16 for x in (q, k, v)), lambda: "q, k, v must be bfloat16")
+    torch._check(0 <= config <= 3, lambda: f"config must be 0..3, got {config}")
+
+
+@torch.library.custom_op("fav4::bshd_forward", mutates_args=(), device_types="cuda")
+def bshd_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, config: int, scale: float,
+                 return_lse: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    _check(q, k, v, config)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    o = torch.empty_like(q)
+    b, sq, h, _ = q.shape
+    lse = torch.empty((b, h, sq) if return_lse else (0,), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        _runner().call(q, k, v, o, lse if return_lse else None, causal, config,
+                       1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale)
+    return o, lse
+
+
+@bshd_forward.register_fake
+def _(q, k, v, causal, config, scale, return_lse):
+    _check(q, k, v, config)
+    b, sq, h, _ = q.shape
+    o = torch.empty_like(q, memory_format=torch.contiguous_format)
+    lse = q.new_empty((b, h, sq) if return_lse else (0,), dtype=torch.float32)
+    return o, lse
+
+
+def attention(q, k, v, causal: bool = False, config: int = 0, scale: float | None = None,
+              return_lse: bool = False):
+    """Convenience wrapper: O, or (O, LSE) when ``return_lse``."""
+    o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, -1.0 if scale is None else scale, return_lse)
+    return (o, lse) if return_lse else o

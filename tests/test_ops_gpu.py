@@ -1,0 +1,76 @@
+"""GPU tests of ``torch.ops.fav4.bshd_forward``: bit-identical to the C ABI
+call it wraps, torch.library.opcheck, use inside a torch.compile graph and in
+a captured CUDA graph, and no silent gradient."""
+import math
+
+import pytest
+import torch
+
+import fav4_bshd as F
+from fav4_bshd import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(b, h, sq, sk, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    return [torch.randn(s, generator=gen, device="cuda", dtype=torch.bfloat16)
+            for s in ((b, sq, h, 128), (b, sk, h, 128), (b, sk, h, 128))]
+
+
+@pytest.mark.parametrize("b,h,sq,sk", [(2, 4, 300, 517), (1, 8, 1024, 1024), (3, 2, 77, 77)])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("config", [0, 1, 3])
+def test_op_matches_c_abi(runner, b, h, sq, sk, causal, config):
+    q, k, v = _inputs(b, h, sq, sk, seed=b + sq)
+    o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, -1.0, True)
+    want_o = torch.empty_like(q)
+    want_l = torch.empty((b, h, sq), device="cuda")
+    runner.call(q, k, v, want_o, want_l, causal, config, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert torch.equal(o, want_o) and torch.equal(lse, want_l)
+    o2 = ops.attention(q, k, v, causal=causal, config=config, scale=0.07)
+    runner.call(q, k, v, want_o, None, causal, config, 0.07)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, want_o)
+
+
+def test_opcheck():
+    q, k, v = _inputs(2, 3, 200, 300, seed=5)
+    for causal, lse in ((False, True), (True, False)):
+        torch.library.opcheck(torch.ops.fav4.bshd_forward.default, (q, k, v, causal, 0, -1.0, lse))
+
+
+def test_inside_torch_compile_graph():
+    q, k, v = _inputs(2, 4, 256, 256, seed=6)
+
+    def block(q, k, v):
+        o = ops.attention(q * 0.5, k, v, causal=True)
+        return o.float().sum(dim=-1)
+
+    want = block(q, k, v)
+    got = torch.compile(block, fullgraph=True)(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+def test_cuda_graph_capture_replays():
+    q, k, v = _inputs(2, 4, 384, 384, seed=7)
+    ops.attention(q, k, v)  # first call on the device happens outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = ops.attention(q, k, v, causal=True)
+    want = ops.attention(q, k, v, causal=True)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+
+
+def test_gradient_is_not_silent():
+    q, k, v = _inputs(1, 2, 128, 128, seed=8)
+    q.requires_grad_(True)
+    with pytest.raises(RuntimeError):
+        o = ops.attention(q, k, v)
+        o.float().sum().backward()
