@@ -47,6 +47,7 @@ struct FwdParams {
   __nv_bfloat16* o;
   float* lse;
   int batch, heads, sq, sk;
+  int kv_group;          // query heads per K/V head (1 unless grouped-query attention)
   int kv_begin, kv_end;  // keys [kv_begin, kv_end) are attended (split-KV slices)
   float scale_log2;      // scale * log2(e)
   int num_mblocks;       // query blocks of QTILES*128 rows per (batch, head)
@@ -286,6 +287,7 @@ __global__ void __launch_bounds__(384, 1)
         if (!mbar_wait(bar(L::kQEmpty), q_empty_par, ctl, kStatusTimeoutLoad)) { ok = false; break; }
         q_empty_par ^= 1u;
         const int nq = (n0 > 0 ? 1 : 0) + (n1 > 0 ? 1 : 0);
+        const int kvh = tc.h / p.kv_group;  // K/V head shared by this query head's group
         mbar_arrive_expect_tx(bar(L::kQFull), nq * kTileBytes);
         for (int i = 0; i < QTiles; ++i) {
           if ((i == 0 ? n0 : n1) == 0) continue;
@@ -306,13 +308,13 @@ __global__ void __launch_bounds__(384, 1)
           const uint32_t dst = sbase + L::kKV + ring.stage * L::kSlotBytes;
           if (has_v) {
             const int sv = p.kv_begin + g * kBlockN;
-            tma_load_4d(dst, &tm_v, fb, 0, tc.h, sv, tc.b, pol_kv);
-            tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, tc.h, sv, tc.b, pol_kv);
+            tma_load_4d(dst, &tm_v, fb, 0, kvh, sv, tc.b, pol_kv);
+            tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, kvh, sv, tc.b, pol_kv);
           }
           if (has_k) {
             const int sk0 = p.kv_begin + (g + 1) * kBlockN;
-            tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, tc.h, sk0, tc.b, pol_kv);
-            tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, tc.h, sk0, tc.b, pol_kv);
+            tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, kvh, sk0, tc.b, pol_kv);
+            tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, kvh, sk0, tc.b, pol_kv);
           }
           ring.advance<Slots>();
         }

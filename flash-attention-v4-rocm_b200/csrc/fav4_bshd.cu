@@ -84,7 +84,7 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
 template <bool Causal, int QTiles, int Slots, int PolyPer8>
-int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream) {
+int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -103,8 +103,8 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
     }
   }
   CUtensorMap tq, tk, tv, to;
-  if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, a.heads) ||
-      !encode_bshd(&tv, a.v, a.batch, a.sk, a.heads) || !encode_bshd(&to, a.o, a.batch, a.sq, a.heads))
+  if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, kv_heads) ||
+      !encode_bshd(&tv, a.v, a.batch, a.sk, kv_heads) || !encode_bshd(&to, a.o, a.batch, a.sq, a.heads))
     return cudaErrorInvalidValue;
   FwdParams p;
   p.o = static_cast<__nv_bfloat16*>(a.o);
@@ -113,6 +113,7 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
   p.heads = a.heads;
   p.sq = a.sq;
   p.sk = a.sk;
+  p.kv_group = a.heads / kv_heads;
   p.kv_begin = kv_begin;
   p.kv_end = kv_end;
   p.scale_log2 = a.scale * 1.4426950408889634f;
@@ -128,11 +129,12 @@ int launch_fwd(const Fav4Args& a, int kv_begin, int kv_end, cudaStream_t stream)
 }
 
 template <bool Causal>
-int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream) {
+int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream, int kv_heads = 0) {
+  if (kv_heads == 0) kv_heads = a.heads;
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_begin, kv_end, stream);
-    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_begin, kv_end, stream);
-    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_begin, kv_end, stream);
+    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_heads, kv_begin, kv_end, stream);
+    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_heads, kv_begin, kv_end, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_heads, kv_begin, kv_end, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -147,6 +149,15 @@ extern "C" int fav4_bshd_forward(const Fav4Args* a, int causal, int config, cuda
   if (config == 0) config = fav4_bshd_select_config(a);
   return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream)
                 : fav4::dispatch<false>(*a, config, 0, a->sk, stream);
+}
+
+extern "C" int fav4_bshd_forward_gqa(const Fav4Args* a, int kv_heads, int causal, int config,
+                                     cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || kv_heads < 1 || kv_heads > a->heads || a->heads % kv_heads)
+    return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream, kv_heads)
+                : fav4::dispatch<false>(*a, config, 0, a->sk, stream, kv_heads);
 }
 
 extern "C" int fav4_bshd_forward_partial(const Fav4Args* a, int causal, int config, int kv_begin, int kv_end,

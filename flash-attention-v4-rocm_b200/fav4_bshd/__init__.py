@@ -43,6 +43,8 @@ def _bind(lib):
     lib.fav4_bshd_forward.restype = C.c_int
     lib.fav4_bshd_select_config.argtypes = [C.POINTER(Args)]
     lib.fav4_bshd_select_config.restype = C.c_int
+    lib.fav4_bshd_forward_gqa.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_forward_gqa.restype = C.c_int
     lib.fav4_bshd_forward_partial.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_partial.restype = C.c_int
     lib.fav4_bshd_combine.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int, C.c_void_p,
@@ -105,11 +107,12 @@ def _stream(stream=None):
     return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
 
 
-def _check_bshd(q, k, v, o, lse):
+def _check_bshd(q, k, v, o, lse, kv_heads=None):
     import torch
     assert all(x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous() for x in (q, k, v, o))
     b, sq, h, d = q.shape
-    assert d == HEAD_DIM and k.shape == v.shape and k.shape[0] == b and k.shape[2:] == (h, d) and o.shape == q.shape
+    hk = h if kv_heads is None else kv_heads
+    assert d == HEAD_DIM and k.shape == v.shape and k.shape[0] == b and k.shape[2:] == (hk, d) and o.shape == q.shape
     assert lse is None or (lse.shape == (b, h, sq) and lse.is_contiguous() and lse.dtype == torch.float32)
     return b, sq, h
 
@@ -130,6 +133,17 @@ class Runner:
         status = self.lib.fav4_bshd_forward(C.byref(a), int(causal), config, _stream(stream))
         if status:
             raise RuntimeError(f"config {config}: CUDA status {status}")
+
+    def call_gqa(self, q, k, v, o, lse, causal, config=0, scale=None, stream=None):
+        """Grouped-query attention: k and v have H_kv heads, H_kv dividing q's
+        heads (fav4_bshd_forward_gqa)."""
+        hk = k.shape[2]
+        b, sq, h = _check_bshd(q, k, v, o, lse, kv_heads=hk)
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        a = Args(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, h, sq, k.shape[1], scale)
+        status = self.lib.fav4_bshd_forward_gqa(C.byref(a), hk, int(causal), config, _stream(stream))
+        if status:
+            raise RuntimeError(f"gqa kv_heads {hk} config {config}: CUDA status {status}")
 
     def call_partial(self, q, k, v, o, lse, causal, kv_begin, kv_end, config=0, scale=None, stream=None):
         a = self.args(q, k, v, o, lse, scale)

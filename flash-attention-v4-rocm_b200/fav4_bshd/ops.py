@@ -8,7 +8,9 @@ output allocation, the current stream and tracing:
     o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, scale, return_lse)
 
 * q, k, v: CUDA BF16 ``[B, S, H, 128]``, contiguous (the reference contract,
-  include/fav4_bshd.h:12-15); k and v share their shape.
+  include/fav4_bshd.h:12-15); k and v share their shape. k and v may have
+  fewer heads than q, a divisor of q's (grouped-query attention, through
+  fav4_bshd_forward_gqa).
 * causal: top-left causal mask. config: 0 (Auto) to 3. scale: softmax scale,
   or a non-positive value for 1/sqrt(128).
 * Returns O (BF16, q's shape) and LSE (FP32 ``[B, H, Sq]``, natural log), or
@@ -41,8 +43,9 @@ def _runner() -> Runner:
 def _check(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config: int) -> None:
     torch._check(q.dim() == 4 and q.shape[-1] == HEAD_DIM, lambda: f"q must be [B, S, H, {HEAD_DIM}], got {q.shape}")
     torch._check(k.shape == v.shape, lambda: f"k and v shapes differ: {k.shape} vs {v.shape}")
-    torch._check(k.dim() == 4 and k.shape[0] == q.shape[0] and k.shape[2:] == q.shape[2:],
-                 lambda: f"k must be [B, Sk, H, {HEAD_DIM}] with q's B and H, got {k.shape}")
+    torch._check(k.dim() == 4 and k.shape[0] == q.shape[0] and k.shape[3] == HEAD_DIM and k.shape[2] >= 1
+                 and q.shape[2] % k.shape[2] == 0,
+                 lambda: f"k must be [B, Sk, H_kv, {HEAD_DIM}] with q's B and H_kv dividing q's heads, got {k.shape}")
     torch._check(all(x.dtype == torch.bfloat16 for x in (q, k, v)), lambda: "q, k, v must be bfloat16")
     torch._check(0 <= config <= 3, lambda: f"config must be 0..3, got {config}")
 
@@ -55,9 +58,12 @@ def bshd_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
     o = torch.empty_like(q)
     b, sq, h, _ = q.shape
     lse = torch.empty((b, h, sq) if return_lse else (0,), device=q.device, dtype=torch.float32)
+    sc = 1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale
     with torch.cuda.device(q.device):
-        _runner().call(q, k, v, o, lse if return_lse else None, causal, config,
-                       1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale)
+        if k.shape[2] == h:
+            _runner().call(q, k, v, o, lse if return_lse else None, causal, config, sc)
+        else:
+            _runner().call_gqa(q, k, v, o, lse if return_lse else None, causal, config, sc)
     return o, lse
 
 

@@ -45,6 +45,16 @@ int fav4_bshd_forward(const Fav4Args* args, int causal, int config, cudaStream_t
  * src/bshd.hip:23-25. */
 int fav4_bshd_select_config(const Fav4Args* args);
 
+/* Grouped-query attention (no reference counterpart: the reference requires
+ * equal Q/K/V heads, include/fav4_bshd.h:15). args->heads is the number of
+ * query heads; K and V are BF16 [batch, sk, kv_heads, 128] with kv_heads
+ * dividing args->heads, and query head h attends K/V head
+ * h / (heads / kv_heads) (kv_heads = 1 is multi-query attention). O and LSE
+ * have args->heads heads. kv_heads == heads is fav4_bshd_forward. Other
+ * arguments, validation and return codes as fav4_bshd_forward, plus
+ * cudaErrorInvalidValue when kv_heads is not a divisor of heads. */
+int fav4_bshd_forward_gqa(const Fav4Args* args, int kv_heads, int causal, int config, cudaStream_t stream);
+
 /* Split-KV slice (no reference counterpart; needed because Fav4Args carries
  * no key offset). Attends only keys [kv_begin, kv_end) with absolute
  * positions, so top-left causal masking stays correct for any slice. O is the

@@ -129,13 +129,26 @@ def sample_rows(n: int) -> np.ndarray:
     return np.array(sorted(r for r in rows if 0 <= r < n), dtype=np.int64)
 
 
+def expand_kv(k, heads: int):
+    """Grouped-query attention: K/V with H_kv heads seen by `heads` query
+    heads, query head h reading K/V head h // (heads // H_kv). Returns K/V
+    repeated to `heads` heads (unchanged when they already have them)."""
+    hk = k.shape[2]
+    if hk == heads:
+        return k
+    assert heads % hk == 0, (heads, hk)
+    return np.repeat(k, heads // hk, axis=2)
+
+
 def reference(q, k, v, causal: bool, rows=None, scale: float | None = None):
     """FP64 attention on the CPU, restating benchmarks/bshd.py:90-100.
 
-    q [B,Sq,H,128], k/v [B,Sk,H,128]; `rows` selects query rows (all if None).
+    q [B,Sq,H,128], k/v [B,Sk,H,128] (or H_kv heads dividing H: grouped-query
+    attention, `expand_kv`); `rows` selects query rows (all if None).
     Returns O [B,H,len(rows),128] (FP64) and LSE [B,H,len(rows)] (FP64), the
     same [B,H,rows,...] layout as the reference's permuted result.
     """
+    k, v = expand_kv(k, q.shape[2]), expand_kv(v, q.shape[2])
     sq = q.shape[1]
     if rows is None:
         rows = np.arange(sq)
@@ -163,6 +176,7 @@ def reference_chunked(q, k, v, causal: bool, rows, scale: float | None = None, m
     """`reference` evaluated one (batch, head) and row chunk at a time, to bound
     memory at long sequence lengths. Same results."""
     b, _, h, _ = q.shape
+    k, v = expand_kv(k, h), expand_kv(v, h)
     rows = np.asarray(rows, dtype=np.int64)
     o = np.empty((b, h, len(rows), D))
     lse = np.empty((b, h, len(rows)))

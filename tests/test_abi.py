@@ -175,3 +175,15 @@ def test_host_forward_rejects_invalid_arguments(lib):
     for h in bad:
         o1 = (F.HostOut * 1)(h)
         assert f(C.byref(a), o1, 1, 2, ws, need, None) == INVALID
+
+
+@pytest.mark.parametrize("kv_heads", [0, -1, 3, 16, 5])
+def test_gqa_rejects_bad_kv_heads(lib, kv_heads):
+    a = make_args(heads=8)
+    assert lib.fav4_bshd_forward_gqa(C.byref(a), kv_heads, 0, 0, None) == INVALID
+
+
+@pytest.mark.parametrize("kw", INVALID_CASES[:14], ids=[str(c) for c in INVALID_CASES[:14]])
+def test_gqa_rejects_invalid_arguments(lib, kw):
+    a = make_args(**kw)
+    assert lib.fav4_bshd_forward_gqa(C.byref(a), 1, 1, 0, None) == INVALID

@@ -38,8 +38,8 @@ def test_fake_rejects_invalid(case):
             q = torch.empty(2, 64, 4, 64, dtype=torch.bfloat16, device="cuda")
         elif case == "kv_mismatch":
             v = torch.empty(2, 65, 4, 128, dtype=torch.bfloat16, device="cuda")
-        elif case == "heads":
-            k = v = torch.empty(2, 64, 2, 128, dtype=torch.bfloat16, device="cuda")
+        elif case == "heads":  # K/V heads must divide the query heads
+            k = v = torch.empty(2, 64, 3, 128, dtype=torch.bfloat16, device="cuda")
         else:
             config = 4
         with pytest.raises(RuntimeError):

@@ -108,3 +108,18 @@ def test_exp2_polynomial_fit_and_kernel_constants():
     assert rel.max() < 1.1e-4
     ints = np.arange(-125, 9, dtype=np.float32)
     assert np.array_equal(R.ex2_poly(ints), np.exp2(ints))
+
+
+def test_grouped_query_reference_is_repeated_kv():
+    """Grouped-query attention in the oracle: query head h reads K/V head
+    h // (H / H_kv), which equals ordinary attention on repeated K/V."""
+    q, _, _ = R.inputs(2, 6, 40, 40, "normal", seed=9)
+    _, k, v = R.inputs(2, 2, 40, 56, "normal", seed=10)
+    assert R.expand_kv(k, 6).shape == (2, 56, 6, 128)
+    assert np.array_equal(R.expand_kv(k, 6)[:, :, 2], k[:, :, 0]) and np.array_equal(R.expand_kv(k, 6)[:, :, 3], k[:, :, 1])
+    for causal in (False, True):
+        o, lse = R.reference(q, k, v, causal)
+        o2, lse2 = R.reference(q, np.repeat(k, 3, axis=2), np.repeat(v, 3, axis=2), causal)
+        assert np.array_equal(o, o2) and np.array_equal(lse, lse2)
+        oc, lc = R.reference_chunked(q, k, v, causal, np.arange(40), max_elems=512)
+        np.testing.assert_allclose(oc, o, rtol=1e-12, atol=1e-12)
