@@ -49,20 +49,30 @@ struct FwdParams {
   int batch, heads, sq, sk;
   int kv_group;          // query heads per K/V head (1 unless grouped-query attention)
   int kv_begin, kv_end;  // keys [kv_begin, kv_end) are attended (split-KV slices)
+  int splits;            // KV splits inside this launch (1 = none): split s attends
+  int kv_chunk;          //   [kv_begin + s*kv_chunk, min(kv_end, kv_begin + (s+1)*kv_chunk)) and
+                         //   writes its partial O / LSE to slice s of o / lse
   float scale_log2;      // scale * log2(e)
   int num_mblocks;       // query blocks of QTILES*128 rows per (batch, head)
-  int num_tiles;         // batch * heads * num_mblocks
+  int num_base_tiles;    // batch * heads * num_mblocks
+  int num_tiles;         // num_base_tiles * splits
   uint32_t* status;
   uint64_t wait_limit_ns;
 };
 
 struct TileCoord {
-  int b, h, m0;  // m0 = first query row of the work tile
+  int b, h, m0;          // m0 = first query row of the work tile
+  int split;             // KV split of the work tile
+  int kv_begin, kv_end;  // keys it attends
 };
 
 template <bool Causal, int QTiles>
 __device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
   TileCoord c;
+  c.split = t / p.num_base_tiles;  // splits outermost
+  t -= c.split * p.num_base_tiles;
+  c.kv_begin = p.kv_begin + c.split * p.kv_chunk;
+  c.kv_end = min(p.kv_end, c.kv_begin + p.kv_chunk);
   if (Causal) {
     const int per_batch = p.heads * p.num_mblocks;
     c.b = t / per_batch;
@@ -78,14 +88,14 @@ __device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
   return c;
 }
 
-// Number of K/V tiles Q tile `i` of a work tile needs (0 = tile skipped).
+// Number of K/V tiles the Q tile at row r0 of work tile `c` needs (0 = tile skipped).
 template <bool Causal>
-__device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int r0) {
+__device__ __forceinline__ int kv_tiles_for(const FwdParams& p, const TileCoord& c, int r0) {
   if (r0 >= p.sq) return 0;  // no real query row in this Q tile
-  int hi = p.kv_end;
+  int hi = c.kv_end;
   if (Causal) hi = min(hi, r0 + kBlockM);  // top-left causal: key c visible to row r iff c <= r
-  if (hi <= p.kv_begin) return 0;
-  return (hi - p.kv_begin + kBlockN - 1) / kBlockN;
+  if (hi <= c.kv_begin) return 0;
+  return (hi - c.kv_begin + kBlockN - 1) / kBlockN;
 }
 
 // Shared memory: Q tiles, then a ring of 64 KiB slots, then barriers. Per work
@@ -280,8 +290,8 @@ __global__ void __launch_bounds__(384, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
-        const int n0 = kv_tiles_for<Causal>(p, tc.m0);
-        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc.m0 + kBlockM) : 0;
+        const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
+        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
         if (N == 0) continue;
         if (!mbar_wait(bar(L::kQEmpty), q_empty_par, ctl, kStatusTimeoutLoad)) { ok = false; break; }
@@ -307,12 +317,12 @@ __global__ void __launch_bounds__(384, 1)
           armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
           const uint32_t dst = sbase + L::kKV + ring.stage * L::kSlotBytes;
           if (has_v) {
-            const int sv = p.kv_begin + g * kBlockN;
+            const int sv = tc.kv_begin + g * kBlockN;
             tma_load_4d(dst, &tm_v, fb, 0, kvh, sv, tc.b, pol_kv);
             tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, kvh, sv, tc.b, pol_kv);
           }
           if (has_k) {
-            const int sk0 = p.kv_begin + (g + 1) * kBlockN;
+            const int sk0 = tc.kv_begin + (g + 1) * kBlockN;
             tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, kvh, sk0, tc.b, pol_kv);
             tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, kvh, sk0, tc.b, pol_kv);
           }
@@ -370,8 +380,8 @@ __global__ void __launch_bounds__(384, 1)
       };
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
-        const int n0 = kv_tiles_for<Causal>(p, tc.m0);
-        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc.m0 + kBlockM) : 0;
+        const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
+        const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
         if (N == 0) continue;
         if (!mbar_wait(bar(L::kQFull), q_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
@@ -447,7 +457,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
       const int r0 = tc.m0 + i * kBlockM;
-      const int ni = kv_tiles_for<Causal>(p, r0);
+      const int ni = kv_tiles_for<Causal>(p, tc, r0);
       const int grow = r0 + row;  // query row (global within the sequence)
       float m = -INFINITY, l = 0.f;
       if (ni == 0) {
@@ -464,11 +474,11 @@ __global__ void __launch_bounds__(384, 1)
         float s[128];
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c / 32][c % 32]);
-        const int col0 = p.kv_begin + j * kBlockN;
+        const int col0 = tc.kv_begin + j * kBlockN;
         // Mask keys past kv_end, and (causal) keys after this row.
-        const bool masked = (col0 + kBlockN > p.kv_end) || (Causal && (col0 + kBlockN - 1 > r0));
+        const bool masked = (col0 + kBlockN > tc.kv_end) || (Causal && (col0 + kBlockN - 1 > r0));
         if (masked) {
-          int lim = p.kv_end - 1 - col0;  // last visible column index within the tile
+          int lim = tc.kv_end - 1 - col0;  // last visible column index within the tile
           if (Causal) lim = min(lim, grow - col0);
 #pragma unroll
           for (int c = 0; c < 128; ++c) s[c] = c > lim ? -INFINITY : s[c];
@@ -557,21 +567,21 @@ __global__ void __launch_bounds__(384, 1)
           fence_proxy_async_smem();
           pair_all(1 + i, 128, true);  // every row of this half is staged
           if (issuer) {
-            tma_store_4d(&tm_o, stage, half * 64, tc.h, r0, tc.b);
+            tma_store_4d(&tm_o, stage, half * 64, tc.h, r0, tc.split * p.batch + tc.b);  // O map: splits x batch
             tma_store_commit();
             if (half == 0) tma_store_wait_read_all();
           }
         }
       } else if (live) {
         // no key visible to this Q tile (a split-KV slice): O = 0
-        uint4* dst = reinterpret_cast<uint4*>(p.o + ((static_cast<int64_t>(tc.b) * p.sq + grow) * p.heads + tc.h) *
-                                                        kHeadDim);
+        const int64_t bs = static_cast<int64_t>(tc.split) * p.batch + tc.b;  // batch row in the split slices
+        uint4* dst = reinterpret_cast<uint4*>(p.o + ((bs * p.sq + grow) * p.heads + tc.h) * kHeadDim);
 #pragma unroll
         for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0u, 0u, 0u, 0u);
       }
       if (!ok) break;
       if (live && p.lse != nullptr) {
-        p.lse[(static_cast<int64_t>(tc.b) * p.heads + tc.h) * p.sq + grow] =
+        p.lse[((static_cast<int64_t>(tc.split) * p.batch + tc.b) * p.heads + tc.h) * p.sq + grow] =
             l > 0.f ? m * kLn2 + logf(l) : -INFINITY;
       }
     }

@@ -84,7 +84,7 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
 template <bool Causal, int QTiles, int Slots, int PolyPer8>
-int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, cudaStream_t stream) {
+int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int splits, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -104,7 +104,7 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, cudaSt
   }
   CUtensorMap tq, tk, tv, to;
   if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, kv_heads) ||
-      !encode_bshd(&tv, a.v, a.batch, a.sk, kv_heads) || !encode_bshd(&to, a.o, a.batch, a.sq, a.heads))
+      !encode_bshd(&tv, a.v, a.batch, a.sk, kv_heads) || !encode_bshd(&to, a.o, a.batch * splits, a.sq, a.heads))
     return cudaErrorInvalidValue;
   FwdParams p;
   p.o = static_cast<__nv_bfloat16*>(a.o);
@@ -116,10 +116,15 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, cudaSt
   p.kv_group = a.heads / kv_heads;
   p.kv_begin = kv_begin;
   p.kv_end = kv_end;
+  p.splits = splits;
+  // whole 128-key tiles per split
+  p.kv_chunk = ((kv_end - kv_begin + splits - 1) / splits + kBlockN - 1) / kBlockN * kBlockN;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.num_mblocks = (a.sq + QTiles * kBlockM - 1) / (QTiles * kBlockM);
-  const int64_t tiles = static_cast<int64_t>(a.batch) * a.heads * p.num_mblocks;
+  const int64_t base = static_cast<int64_t>(a.batch) * a.heads * p.num_mblocks;
+  const int64_t tiles = base * splits;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
+  p.num_base_tiles = static_cast<int>(base);
   p.num_tiles = static_cast<int>(tiles);
   p.status = info.status;
   p.wait_limit_ns = wait_limit_ns();
@@ -129,12 +134,13 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, cudaSt
 }
 
 template <bool Causal>
-int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream, int kv_heads = 0) {
+int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream, int kv_heads = 0,
+             int splits = 1) {
   if (kv_heads == 0) kv_heads = a.heads;
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_heads, kv_begin, kv_end, stream);
-    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_heads, kv_begin, kv_end, stream);
-    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_heads, kv_begin, kv_end, stream);
+    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_heads, kv_begin, kv_end, splits, stream);
+    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_heads, kv_begin, kv_end, splits, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_heads, kv_begin, kv_end, splits, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -416,6 +422,95 @@ extern "C" int fav4_bshd_forward_host(const Fav4Args* a, const Fav4HostOut* outs
   // one stream complete in order, so the last one covers the others).
   const cudaError_t j = cudaStreamWaitEvent(stream, pipe.downloaded[last], 0);
   return e != cudaSuccess ? e : j;
+}
+
+// --------------------------------------------------------------------------
+// Split-KV in one launch, for shapes with few query tiles (decoding: Sq much
+// smaller than Sk). The kernel's work tiles gain a split index; split s
+// writes its partial O (normalised within the split) and LSE to slice s of a
+// caller-provided workspace, and the LSE-weighted combine kernel merges the
+// slices into O and LSE.
+namespace fav4 {
+namespace {
+
+struct SplitLayout {
+  size_t o_slice = 0, lse_slice = 0;  // bytes of one split's partial O / LSE (rounded to 256)
+};
+
+SplitLayout split_layout(const Fav4Args* a) {
+  SplitLayout l;
+  const size_t rows = static_cast<size_t>(a->batch) * a->sq * a->heads;
+  l.o_slice = round256(rows * kHeadDim * 2);
+  l.lse_slice = round256(rows * 4);
+  return l;
+}
+
+// Query tiles of the work decomposition the config uses.
+int64_t base_tiles(const Fav4Args* a, int config) {
+  const int rows = config == 1 ? kBlockM : 2 * kBlockM;
+  return static_cast<int64_t>(a->batch) * a->heads * ((a->sq + rows - 1) / rows);
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_splitkv_splits(const Fav4Args* a, int causal, int config) {
+  if (!fav4::args_valid(a, causal, config)) return -1;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  fav4::DeviceInfo info;
+  if (!fav4::device_info(dev, &info)) return -1;
+  const int64_t base = fav4::base_tiles(a, config);
+  // keys any query row can see (top-left causal: rows < sq see keys < sq)
+  const int keys = causal ? (a->sq < a->sk ? a->sq : a->sk) : a->sk;
+  const int64_t kv_tiles = (keys + fav4::kBlockN - 1) / fav4::kBlockN;
+  // enough work tiles to fill the SMs, at least 4 K/V tiles (512 keys) per split, at most 16 splits
+  int64_t splits = (info.sms + base - 1) / base;
+  if (splits > kv_tiles / 4) splits = kv_tiles / 4;
+  if (splits > fav4::kMaxCombineParts) splits = fav4::kMaxCombineParts;
+  return splits < 1 ? 1 : static_cast<int>(splits);
+}
+
+extern "C" size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* a, int splits) {
+  if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || splits < 1 || splits > fav4::kMaxCombineParts ||
+      a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128))
+    return 0;
+  if (splits == 1) return 0;
+  const fav4::SplitLayout l = fav4::split_layout(a);
+  return static_cast<size_t>(splits) * (l.o_slice + l.lse_slice);
+}
+
+extern "C" int fav4_bshd_forward_splitkv(const Fav4Args* a, int causal, int config, int splits, void* workspace,
+                                         size_t workspace_bytes, cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || splits < 0 || splits > fav4::kMaxCombineParts)
+    return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  if (splits == 0) splits = fav4_bshd_splitkv_splits(a, causal, config);
+  if (splits < 1) return cudaErrorInvalidValue;
+  if (splits == 1) return fav4_bshd_forward(a, causal, config, stream);
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < fav4_bshd_splitkv_workspace_bytes(a, splits))
+    return cudaErrorInvalidValue;
+  const fav4::SplitLayout l = fav4::split_layout(a);
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  Fav4Args pa = *a;
+  pa.o = ws;                                                          // [splits][B][Sq][H][128] BF16
+  pa.lse = reinterpret_cast<float*>(ws + splits * l.o_slice);         // [splits][B][H][Sq] FP32
+  // The kernel indexes the slices densely: O slice s starts s * B*Sq*H*128 elements in (exactly
+  // o_slice bytes, a multiple of 256), LSE slice s starts s * B*H*Sq values into the LSE region.
+  const size_t o_elems = static_cast<size_t>(a->batch) * a->sq * a->heads * fav4::kHeadDim;
+  const size_t lse_elems = static_cast<size_t>(a->batch) * a->heads * a->sq;
+  const void* o_parts[fav4::kMaxCombineParts];
+  const float* lse_parts[fav4::kMaxCombineParts];
+  for (int s = 0; s < splits; ++s) {
+    o_parts[s] = ws + s * o_elems * 2;
+    lse_parts[s] = reinterpret_cast<const float*>(ws + splits * l.o_slice) + s * lse_elems;
+  }
+  const int e = causal ? fav4::dispatch<true>(pa, config, 0, a->sk, stream, 0, splits)
+                       : fav4::dispatch<false>(pa, config, 0, a->sk, stream, 0, splits);
+  if (e != cudaSuccess) return e;
+  return fav4_bshd_combine(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
 }
 
 extern "C" int fav4_bshd_pipeline_status(int clear) {

@@ -43,6 +43,13 @@ def _bind(lib):
     lib.fav4_bshd_forward.restype = C.c_int
     lib.fav4_bshd_select_config.argtypes = [C.POINTER(Args)]
     lib.fav4_bshd_select_config.restype = C.c_int
+    lib.fav4_bshd_forward_splitkv.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                              C.c_void_p]
+    lib.fav4_bshd_forward_splitkv.restype = C.c_int
+    lib.fav4_bshd_splitkv_workspace_bytes.argtypes = [C.POINTER(Args), C.c_int]
+    lib.fav4_bshd_splitkv_workspace_bytes.restype = C.c_size_t
+    lib.fav4_bshd_splitkv_splits.argtypes = [C.POINTER(Args), C.c_int, C.c_int]
+    lib.fav4_bshd_splitkv_splits.restype = C.c_int
     lib.fav4_bshd_forward_gqa.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_gqa.restype = C.c_int
     lib.fav4_bshd_forward_partial.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
@@ -133,6 +140,30 @@ class Runner:
         status = self.lib.fav4_bshd_forward(C.byref(a), int(causal), config, _stream(stream))
         if status:
             raise RuntimeError(f"config {config}: CUDA status {status}")
+
+    def call_splitkv(self, q, k, v, o, lse, causal, config=0, splits=0, scale=None, stream=None, workspace=None):
+        """Split-KV forward in one launch (fav4_bshd_forward_splitkv), for few
+        query tiles against many keys. splits=0 picks the number for this GPU.
+        The workspace is allocated with torch (kept for the next call) unless
+        one is given. Returns the number of splits used."""
+        import torch
+        a = self.args(q, k, v, o, lse, scale)
+        if splits == 0:
+            splits = self.lib.fav4_bshd_splitkv_splits(C.byref(a), int(causal), config)
+            if splits < 1:
+                raise RuntimeError("splitkv: invalid arguments")
+        need = self.lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), splits)
+        if workspace is None and need > 0:
+            ws = getattr(self, "_split_ws", None)
+            if ws is None or ws.numel() < need or ws.device != q.device:
+                ws = self._split_ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = ws
+        ptr, size = (workspace.data_ptr(), workspace.numel()) if workspace is not None else (None, 0)
+        status = self.lib.fav4_bshd_forward_splitkv(C.byref(a), int(causal), config, splits, ptr, size,
+                                                    _stream(stream))
+        if status:
+            raise RuntimeError(f"splitkv {splits} splits, config {config}: CUDA status {status}")
+        return splits
 
     def call_gqa(self, q, k, v, o, lse, causal, config=0, scale=None, stream=None):
         """Grouped-query attention: k and v have H_kv heads, H_kv dividing q's

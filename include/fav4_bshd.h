@@ -98,6 +98,32 @@ int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts,
 int fav4_bshd_forward_splitkv_static(const Fav4Args* args, int causal, int config, int splits,
                                      cudaStream_t stream);
 
+/* Split-KV forward in one launch, for shapes with few query tiles such as
+ * decoding (Sq much smaller than Sk; no reference counterpart). The keys are
+ * cut into `splits` ranges of whole 128-key tiles; one kernel launch computes
+ * every (query tile, key range) pair, writing per-range partial O and LSE to
+ * `workspace`, and the LSE-weighted combine kernel (fav4_bshd_combine) merges
+ * them into args->o / args->lse. Results equal fav4_bshd_forward within the
+ * split-KV tolerance (|dO| <= 2e-2, |dLSE| <= 1e-3).
+ *   - splits: 1..16, or 0 for fav4_bshd_splitkv_splits(args, causal, config);
+ *     1 is fav4_bshd_forward and needs no workspace.
+ *   - workspace: device memory, 256-byte aligned, at least
+ *     fav4_bshd_splitkv_workspace_bytes(args, splits) bytes; calls sharing a
+ *     workspace must not overlap.
+ * Other arguments and return codes as fav4_bshd_forward. */
+int fav4_bshd_forward_splitkv(const Fav4Args* args, int causal, int config, int splits, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
+
+/* Workspace bytes fav4_bshd_forward_splitkv needs for `splits` (0 for 1 split
+ * or invalid arguments). */
+size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* args, int splits);
+
+/* The automatic number of splits on the current device: enough work tiles to
+ * cover its SMs, at least 4 key tiles (512 keys) per split, at most 16. Returns
+ * 1 when the query tiles alone fill the GPU, -1 on invalid arguments or a CUDA
+ * error. */
+int fav4_bshd_splitkv_splits(const Fav4Args* args, int causal, int config);
+
 /* One output of fav4_bshd_forward_host: host buffers for O (BF16
  * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and
  * the mask and config it is computed with. */

@@ -187,3 +187,28 @@ def test_gqa_rejects_bad_kv_heads(lib, kv_heads):
 def test_gqa_rejects_invalid_arguments(lib, kw):
     a = make_args(**kw)
     assert lib.fav4_bshd_forward_gqa(C.byref(a), 1, 1, 0, None) == INVALID
+
+
+def test_splitkv_workspace_bytes(lib):
+    a = make_args(batch=2, heads=8, sq=16, sk=4096)
+    r256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    per = r256(2 * 16 * 8 * 256) + r256(2 * 8 * 16 * 4)
+    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 5) == 5 * per
+    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 1) == 0
+    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 0) == 0
+    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 17) == 0
+
+
+def test_splitkv_rejects_invalid_arguments(lib):
+    a = make_args(batch=1, heads=8, sq=16, sk=4096)
+    need = lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 4)
+    f = lib.fav4_bshd_forward_splitkv
+    ws = A16 * 256
+    assert f(C.byref(a), 0, 0, 17, ws, need, None) == INVALID
+    assert f(C.byref(a), 0, 0, -1, ws, need, None) == INVALID
+    assert f(C.byref(a), 0, 0, 4, ws, need - 1, None) == INVALID      # workspace too small
+    assert f(C.byref(a), 0, 0, 4, ws + 128, need, None) == INVALID    # misaligned
+    assert f(C.byref(a), 0, 0, 4, None, need, None) == INVALID
+    assert f(C.byref(a), 2, 0, 4, ws, need, None) == INVALID          # bad mode
+    b = make_args(q=None)
+    assert f(C.byref(b), 0, 0, 4, ws, need, None) == INVALID
