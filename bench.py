@@ -350,6 +350,121 @@ def run_compare(args):
         torch.cuda.empty_cache()
 
 
+def run_decode(args):
+    """Decode-like shapes on one GPU (few query rows against a long key cache):
+    fav4_bshd_forward against the one-launch split-KV forward with the
+    automatic split count, on the same tensors. One JSON line per shape with
+    both times, the split count, and the K/V bytes read per microsecond (the
+    path is HBM-bound: every key and value is read once)."""
+    import torch
+
+    import fav4_bshd
+    runner = fav4_bshd.Runner()
+    pk, pk_kind = peaks()
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    for sk in [int(x) for x in args.decode_sk.split(",")]:
+        for sq in [int(x) for x in args.decode_sq.split(",")]:
+            b, h = 1, H
+            q = torch.randn((b, sq, h, D), generator=gen, device="cuda", dtype=torch.bfloat16)
+            k, v = (torch.randn((b, sk, h, D), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+            o = torch.empty_like(q)
+            o_split = torch.empty_like(q)
+            used = runner.call_splitkv(q, k, v, o_split, None, False, args.config, 0)
+            runner.call(q, k, v, o, None, False, args.config)
+            torch.cuda.synchronize()
+            diff = float((o.float() - o_split.float()).abs().max())
+
+            def timed(fn):
+                for _ in range(max(3, args.warmup)):
+                    fn()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.steps):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) * 1e3 / args.steps
+
+            us_plain = timed(lambda: runner.call(q, k, v, o, None, False, args.config))
+            us_split = timed(lambda: runner.call_splitkv(q, k, v, o_split, None, False, args.config, used))
+            kv_bytes = 2 * b * sk * h * D * 2
+            emit({"mode": "decode", "batch": b, "heads": h, "sq": sq, "sk": sk, "splits": used,
+                  "us_forward": us_plain, "us_splitkv": us_split, "speedup": us_plain / us_split,
+                  "kv_gbs_splitkv": kv_bytes / us_split / 1e3,
+                  "frac_of_measured_hbm": kv_bytes / us_split / 1e3 / pk["hbm_gbs"], "peak_source": pk_kind,
+                  "max_abs_diff": diff, "config": args.config,
+                  "note": "each call re-reads K/V from HBM (K/V are larger than L2 from sk=32768)"})
+            del q, k, v, o, o_split
+            torch.cuda.empty_cache()
+
+
+def run_decode_multi(args, rank, world, local):
+    """Decode step across the N ranks of this torchrun job (fav4_bshd.splitkv.
+    DecodeSplitKV): B1 H8, the first --decode-sq query rows against the last
+    --decode-sk keys, one contiguous key chunk per GPU, combine over NVLink
+    peer reads. Times K steps (device events, max over ranks), checks every
+    rank's full output against one GPU's split-KV forward. One JSON line."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import fav4_bshd
+    from fav4_bshd.splitkv import DecodeSplitKV
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        b, h = 1, H
+        sq = int(args.decode_sq.split(",")[0])
+        sk = int(args.decode_sk.split(",")[-1])
+        gen = torch.Generator(device=dev).manual_seed(4)  # same inputs on every rank
+        q = torch.randn((b, sq, h, D), generator=gen, device=dev, dtype=torch.bfloat16)
+        k, v = (torch.randn((b, sk, h, D), generator=gen, device=dev, dtype=torch.bfloat16) for _ in range(2))
+        dec = DecodeSplitKV(dist.group.WORLD, b, h, sq, sk, dev, causal=False, config=args.config)
+        for _ in range(max(1, args.warmup)):
+            dec.forward(q, k, v)
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            o, lse = dec.forward(q, k, v)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+        one_o = torch.empty_like(q)
+        one_l = torch.empty((b, h, sq), device=dev, dtype=torch.float32)
+        runner = fav4_bshd.Runner()
+        one_splits = runner.call_splitkv(q, k, v, one_o, one_l, False, args.config, 0)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            runner.call_splitkv(q, k, v, one_o, one_l, False, args.config, one_splits)
+        e1.record()
+        torch.cuda.synchronize()
+        us_one = e0.elapsed_time(e1) * 1e3 / args.steps
+        err = torch.tensor([(o.float() - one_o.float()).abs().max().item(), (o.float() - one_o.float()).abs().mean().item(),
+                            (lse - one_l).abs().max().item()], device=dev, dtype=torch.float64)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            kv_bytes = 2 * b * sk * h * D * 2
+            emit({"mode": "decode_split_kv", "metric": "decode step time (B1 H8 D128), key cache split over GPUs",
+                  "us_per_step": us, "n_gpus": world, "steps": args.steps, "sq": sq, "sk": sk,
+                  "splits_per_gpu": dec.splits, "kv_gbs_aggregate": kv_bytes / us / 1e3,
+                  "single_gpu_us": us_one, "speedup_vs_single_gpu": us_one / us, "config": args.config,
+                  "vs_single_gpu": {"max_abs_o": err[0].item(), "mean_abs_o": err[1].item(),
+                                    "max_abs_lse": err[2].item(),
+                                    "within_tolerance": bool(err[0] <= 2e-2 and err[1] <= 2e-3 and err[2] <= 1e-3)}})
+        del dec
+    finally:
+        dist.destroy_process_group()
+
+
 def run_long_context(args, rank, world, local):
     """B1 H8 S131072 causal, KV split over the N ranks of
     this torchrun job (fav4_bshd.splitkv: zigzag chunks, combine over NVLink
@@ -421,6 +536,10 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="profiling only: per-GPU batch")
     ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
     ap.add_argument("--sweep", action="store_true", help="BASELINE configs[2] sequence sweep, one GPU")
+    ap.add_argument("--decode", action="store_true",
+                    help="decode-like shapes (B1 H8, few query rows, long key cache): forward vs one-launch split-KV")
+    ap.add_argument("--decode-sq", default="1,16,64,128")
+    ap.add_argument("--decode-sk", default="8192,32768,131072")
     ap.add_argument("--compare", action="store_true",
                     help="same-box comparison with torch SDPA (cuDNN, flash) and flash_attn, one GPU")
     ap.add_argument("--seqs", default="512,1024,2048,4096,8192,16384,32768")
@@ -434,6 +553,13 @@ def main():
         return
     if args.compare:
         run_compare(args)
+        return
+    if args.decode:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            run_decode_multi(args, int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]),
+                             int(os.environ.get("LOCAL_RANK", "0")))
+        else:
+            run_decode(args)
         return
     if (args.batch, args.seq) != (B, S):
         set_shape(args.batch, args.seq)

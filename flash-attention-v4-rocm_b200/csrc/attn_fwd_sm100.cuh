@@ -66,13 +66,21 @@ struct TileCoord {
   int kv_begin, kv_end;  // keys it attends
 };
 
-template <bool Causal, int QTiles>
+// Split: the launch has a key-range index (p.splits > 1); without it every
+// work tile attends [p.kv_begin, p.kv_end) and the index is a constant 0.
+template <bool Causal, int QTiles, bool Split = false>
 __device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
   TileCoord c;
-  c.split = t / p.num_base_tiles;  // splits outermost
-  t -= c.split * p.num_base_tiles;
-  c.kv_begin = p.kv_begin + c.split * p.kv_chunk;
-  c.kv_end = min(p.kv_end, c.kv_begin + p.kv_chunk);
+  if (Split) {
+    c.split = t / p.num_base_tiles;  // splits outermost
+    t -= c.split * p.num_base_tiles;
+    c.kv_begin = p.kv_begin + c.split * p.kv_chunk;
+    c.kv_end = min(p.kv_end, c.kv_begin + p.kv_chunk);
+  } else {
+    c.split = 0;
+    c.kv_begin = p.kv_begin;
+    c.kv_end = p.kv_end;
+  }
   if (Causal) {
     const int per_batch = p.heads * p.num_mblocks;
     c.b = t / per_batch;
@@ -220,7 +228,7 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 }
 
 // ---------------------------------------------------------------------------
-template <bool Causal, int QTiles, int Slots, int PolyPer8>
+template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t armed_mask = 0, armed_par = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+        const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
@@ -379,7 +387,7 @@ __global__ void __launch_bounds__(384, 1)
         for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
       };
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+        const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
@@ -455,7 +463,7 @@ __global__ void __launch_bounds__(384, 1)
     const float scale_log2 = p.scale_log2;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      const TileCoord tc = tile_coord<Causal, QTiles>(p, t);
+      const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
       const int r0 = tc.m0 + i * kBlockM;
       const int ni = kv_tiles_for<Causal>(p, tc, r0);
       const int grow = r0 + row;  // query row (global within the sequence)

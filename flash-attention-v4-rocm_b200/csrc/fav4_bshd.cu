@@ -83,14 +83,14 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 //   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
-template <bool Causal, int QTiles, int Slots, int PolyPer8>
+template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split>
 int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int splits, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   DeviceInfo info;
   if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
-  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8>;
+  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split>;
   constexpr int smem = SmemLayout<QTiles, Slots>::kAlloc;
   {
     static std::mutex mu;
@@ -137,10 +137,18 @@ template <bool Causal>
 int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream, int kv_heads = 0,
              int splits = 1) {
   if (kv_heads == 0) kv_heads = a.heads;
+  if (splits > 1) {  // the work tiles carry a key-range index
+    switch (config) {
+      case 1: return launch_fwd<Causal, 1, 2, 0, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 2: return launch_fwd<Causal, 2, 2, 2, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 3: return launch_fwd<Causal, 2, 2, 4, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 2, 0>(a, kv_heads, kv_begin, kv_end, splits, stream);
-    case 2: return launch_fwd<Causal, 2, 2, 2>(a, kv_heads, kv_begin, kv_end, splits, stream);
-    case 3: return launch_fwd<Causal, 2, 2, 4>(a, kv_heads, kv_begin, kv_end, splits, stream);
+    case 1: return launch_fwd<Causal, 1, 2, 0, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 2: return launch_fwd<Causal, 2, 2, 2, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 4, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -481,6 +489,40 @@ extern "C" size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* a, int split
   return static_cast<size_t>(splits) * (l.o_slice + l.lse_slice);
 }
 
+namespace fav4 {
+namespace {
+
+// Keys [kv_begin, kv_end) in `splits` ranges inside one launch, then the LSE
+// combine into a->o / a->lse (args already validated, config resolved).
+int splitkv_range(const Fav4Args* a, int causal, int config, int kv_begin, int kv_end, int splits, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream) {
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < fav4_bshd_splitkv_workspace_bytes(a, splits))
+    return cudaErrorInvalidValue;
+  const SplitLayout l = split_layout(a);
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  Fav4Args pa = *a;
+  pa.o = ws;                                                   // [splits][B][Sq][H][128] BF16
+  pa.lse = reinterpret_cast<float*>(ws + splits * l.o_slice);  // [splits][B][H][Sq] FP32
+  // The kernel indexes the slices densely: O slice s starts s * B*Sq*H*128 elements in (exactly
+  // o_slice bytes, a multiple of 256), LSE slice s starts s * B*H*Sq values into the LSE region.
+  const size_t o_elems = static_cast<size_t>(a->batch) * a->sq * a->heads * kHeadDim;
+  const size_t lse_elems = static_cast<size_t>(a->batch) * a->heads * a->sq;
+  const void* o_parts[kMaxCombineParts];
+  const float* lse_parts[kMaxCombineParts];
+  for (int s = 0; s < splits; ++s) {
+    o_parts[s] = ws + s * o_elems * 2;
+    lse_parts[s] = reinterpret_cast<const float*>(ws + splits * l.o_slice) + s * lse_elems;
+  }
+  const int e = causal ? dispatch<true>(pa, config, kv_begin, kv_end, stream, 0, splits)
+                       : dispatch<false>(pa, config, kv_begin, kv_end, stream, 0, splits);
+  if (e != cudaSuccess) return e;
+  return fav4_bshd_combine(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
+}
+
+}  // namespace
+}  // namespace fav4
+
 extern "C" int fav4_bshd_forward_splitkv(const Fav4Args* a, int causal, int config, int splits, void* workspace,
                                          size_t workspace_bytes, cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || splits < 0 || splits > fav4::kMaxCombineParts)
@@ -489,28 +531,18 @@ extern "C" int fav4_bshd_forward_splitkv(const Fav4Args* a, int causal, int conf
   if (splits == 0) splits = fav4_bshd_splitkv_splits(a, causal, config);
   if (splits < 1) return cudaErrorInvalidValue;
   if (splits == 1) return fav4_bshd_forward(a, causal, config, stream);
-  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
-      workspace_bytes < fav4_bshd_splitkv_workspace_bytes(a, splits))
+  return fav4::splitkv_range(a, causal, config, 0, a->sk, splits, workspace, workspace_bytes, stream);
+}
+
+extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, int config, int kv_begin,
+                                                 int kv_end, int splits, void* workspace, size_t workspace_bytes,
+                                                 cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || !a->lse || kv_begin < 0 || kv_end <= kv_begin || kv_end > a->sk ||
+      (reinterpret_cast<uintptr_t>(a->lse) & 3) || splits < 1 || splits > fav4::kMaxCombineParts)
     return cudaErrorInvalidValue;
-  const fav4::SplitLayout l = fav4::split_layout(a);
-  unsigned char* ws = static_cast<unsigned char*>(workspace);
-  Fav4Args pa = *a;
-  pa.o = ws;                                                          // [splits][B][Sq][H][128] BF16
-  pa.lse = reinterpret_cast<float*>(ws + splits * l.o_slice);         // [splits][B][H][Sq] FP32
-  // The kernel indexes the slices densely: O slice s starts s * B*Sq*H*128 elements in (exactly
-  // o_slice bytes, a multiple of 256), LSE slice s starts s * B*H*Sq values into the LSE region.
-  const size_t o_elems = static_cast<size_t>(a->batch) * a->sq * a->heads * fav4::kHeadDim;
-  const size_t lse_elems = static_cast<size_t>(a->batch) * a->heads * a->sq;
-  const void* o_parts[fav4::kMaxCombineParts];
-  const float* lse_parts[fav4::kMaxCombineParts];
-  for (int s = 0; s < splits; ++s) {
-    o_parts[s] = ws + s * o_elems * 2;
-    lse_parts[s] = reinterpret_cast<const float*>(ws + splits * l.o_slice) + s * lse_elems;
-  }
-  const int e = causal ? fav4::dispatch<true>(pa, config, 0, a->sk, stream, 0, splits)
-                       : fav4::dispatch<false>(pa, config, 0, a->sk, stream, 0, splits);
-  if (e != cudaSuccess) return e;
-  return fav4_bshd_combine(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
+  if (config == 0) config = fav4_bshd_select_config(a);
+  if (splits == 1) return fav4_bshd_forward_partial(a, causal, config, kv_begin, kv_end, stream);
+  return fav4::splitkv_range(a, causal, config, kv_begin, kv_end, splits, workspace, workspace_bytes, stream);
 }
 
 extern "C" int fav4_bshd_pipeline_status(int clear) {

@@ -46,6 +46,9 @@ def _bind(lib):
     lib.fav4_bshd_forward_splitkv.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                                               C.c_void_p]
     lib.fav4_bshd_forward_splitkv.restype = C.c_int
+    lib.fav4_bshd_forward_partial_splitkv.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                      C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.fav4_bshd_forward_partial_splitkv.restype = C.c_int
     lib.fav4_bshd_splitkv_workspace_bytes.argtypes = [C.POINTER(Args), C.c_int]
     lib.fav4_bshd_splitkv_workspace_bytes.restype = C.c_size_t
     lib.fav4_bshd_splitkv_splits.argtypes = [C.POINTER(Args), C.c_int, C.c_int]
@@ -164,6 +167,27 @@ class Runner:
         if status:
             raise RuntimeError(f"splitkv {splits} splits, config {config}: CUDA status {status}")
         return splits
+
+    def _split_workspace(self, a, splits, device):
+        import torch
+        need = self.lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), splits)
+        if need == 0:
+            return None, 0
+        ws = getattr(self, "_split_ws", None)
+        if ws is None or ws.numel() < need or ws.device != device:
+            ws = self._split_ws = torch.empty(need, dtype=torch.uint8, device=device)
+        return ws.data_ptr(), ws.numel()
+
+    def call_partial_splitkv(self, q, k, v, o, lse, causal, kv_begin, kv_end, config=0, splits=1, scale=None,
+                             stream=None):
+        """fav4_bshd_forward_partial over keys [kv_begin, kv_end) with the
+        one-launch split (fav4_bshd_forward_partial_splitkv)."""
+        a = self.args(q, k, v, o, lse, scale)
+        ptr, size = self._split_workspace(a, splits, q.device)
+        status = self.lib.fav4_bshd_forward_partial_splitkv(C.byref(a), int(causal), config, kv_begin, kv_end,
+                                                            splits, ptr, size, _stream(stream))
+        if status:
+            raise RuntimeError(f"partial splitkv [{kv_begin},{kv_end}) x{splits}: CUDA status {status}")
 
     def call_gqa(self, q, k, v, o, lse, causal, config=0, scale=None, stream=None):
         """Grouped-query attention: k and v have H_kv heads, H_kv dividing q's

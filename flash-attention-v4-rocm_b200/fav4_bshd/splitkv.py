@@ -56,6 +56,86 @@ def causal_work(ranges: list[tuple[int, int]], sq: int) -> int:
     return total
 
 
+def contiguous_chunk(sk: int, world: int, rank: int, block: int = BLOCK_N) -> tuple[int, int]:
+    """Keys [begin, end) of `rank` when the keys are cut into `world` contiguous
+    chunks of whole `block`-key tiles (the last ones may be short or empty).
+    Balanced for decode-like steps, where every query row sees every key."""
+    tiles = (sk + block - 1) // block
+    per = (tiles + world - 1) // world
+    begin = min(sk, rank * per * block)
+    return begin, min(sk, begin + per * block)
+
+
+class DecodeSplitKV:
+    """Decode-like step (a few query rows, a long key cache) across the G GPUs
+    of a process group.
+
+    Rank r attends one contiguous chunk of the keys (`contiguous_chunk`) for
+    every query row, split again inside one kernel launch so that its own GPU
+    is filled (fav4_bshd_forward_partial_splitkv), and writes the chunk's
+    partial O and LSE to torch symmetric memory. After a device barrier every
+    rank's combine kernel reads all G partials for all rows directly from the
+    peers' memory over NVLink (plain loads) and writes the full output, so each
+    rank ends with the whole O [B, Sq, H, 128] and LSE [B, H, Sq]; a second
+    barrier keeps the partials alive until every rank has read them. No
+    collective moves data. For causal masking (top-left) the chunks are not
+    balanced; decode steps attend the whole cache.
+    """
+
+    def __init__(self, group, batch: int, heads: int, sq: int, sk: int, device, causal: bool = False,
+                 config: int = 0, splits: int = 0):
+        import ctypes as C
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        import fav4_bshd
+        self.torch = torch
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.b, self.h, self.sq, self.sk = batch, heads, sq, sk
+        self.causal, self.config = causal, config
+        self.runner = fav4_bshd.Runner()
+        self.kv = contiguous_chunk(sk, self.world, self.rank)
+        n = self.kv[1] - self.kv[0]
+        if splits == 0 and n > 0:
+            a = fav4_bshd.Args(16, 32, 48, 64, 80, batch, heads, sq, n, 1.0)
+            splits = max(1, self.runner.lib.fav4_bshd_splitkv_splits(C.byref(a), int(causal), config))
+        self.splits = max(1, splits)
+        self.o_part = symm.empty((batch, sq, heads, 128), dtype=torch.bfloat16, device=device)
+        self.lse_part = symm.empty((batch, heads, sq), dtype=torch.float32, device=device)
+        self.o_hdl = symm.rendezvous(self.o_part, group)
+        self.l_hdl = symm.rendezvous(self.lse_part, group)
+        self.out_o = torch.empty((batch, sq, heads, 128), dtype=torch.bfloat16, device=device)
+        self.out_l = torch.empty((batch, heads, sq), dtype=torch.float32, device=device)
+
+    def partials(self, q, k, v):
+        """This rank's chunk: partial O and LSE of every query row."""
+        if self.kv[1] <= self.kv[0]:
+            self.o_part.zero_()
+            self.lse_part.fill_(-math.inf)
+        else:
+            self.runner.call_partial_splitkv(q, k, v, self.o_part, self.lse_part, self.causal, self.kv[0],
+                                             self.kv[1], self.config, self.splits)
+
+    def exchange_and_combine(self):
+        import ctypes as C
+        self.o_hdl.barrier(channel=0)
+        stream = self.torch.cuda.current_stream().cuda_stream
+        o_ptrs = (C.c_void_p * self.world)(*[self.o_hdl.buffer_ptrs[g] for g in range(self.world)])
+        l_ptrs = (C.c_void_p * self.world)(*[self.l_hdl.buffer_ptrs[g] for g in range(self.world)])
+        status = self.runner.lib.fav4_bshd_combine(o_ptrs, l_ptrs, self.world, self.out_o.data_ptr(),
+                                                   self.out_l.data_ptr(), self.b, self.h, self.sq, stream)
+        if status:
+            raise RuntimeError(f"combine: CUDA status {status}")
+        self.o_hdl.barrier(channel=1)
+        return self.out_o, self.out_l
+
+    def forward(self, q, k, v):
+        self.partials(q, k, v)
+        return self.exchange_and_combine()
+
+
 class SplitKV:
     """Split-KV forward over a process group of GPUs.
 

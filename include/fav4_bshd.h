@@ -114,6 +114,15 @@ int fav4_bshd_forward_splitkv_static(const Fav4Args* args, int causal, int confi
 int fav4_bshd_forward_splitkv(const Fav4Args* args, int causal, int config, int splits, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
 
+/* fav4_bshd_forward_partial with the one-launch split: keys [kv_begin, kv_end)
+ * (absolute positions) in `splits` (1..16) ranges, combined into the slice's
+ * partial O and its LSE (required), as fav4_bshd_forward_partial returns them.
+ * For a GPU that holds one key chunk of a multi-GPU decode step. Validation
+ * and return codes as fav4_bshd_forward_partial, workspace as
+ * fav4_bshd_forward_splitkv. */
+int fav4_bshd_forward_partial_splitkv(const Fav4Args* args, int causal, int config, int kv_begin, int kv_end,
+                                      int splits, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Workspace bytes fav4_bshd_forward_splitkv needs for `splits` (0 for 1 split
  * or invalid arguments). */
 size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* args, int splits);

@@ -5,6 +5,8 @@
   whole causal problem within the north-star tolerance.
 * bench.py's batch-sharded headline run under torchrun prints one JSON line
   with n_gpus = 2 and no pipeline timeouts.
+* The decode split-KV path (fav4_bshd.splitkv.DecodeSplitKV) across 2 ranks:
+  every rank's full output matches one GPU's split-KV forward.
 """
 import json
 import os
@@ -43,3 +45,10 @@ def test_long_context_split_kv_two_gpus():
 def test_batch_sharded_bench_two_gpus():
     out = _torchrun(2, "--gpus", "2", "--steps", "3", "--warmup", "3")
     assert out["n_gpus"] == 2 and out["pipeline_status"] == 0 and out["value"] > 0, out
+
+
+@needs2
+def test_decode_split_kv_two_gpus():
+    out = _torchrun(2, "--decode", "--decode-sq", "16", "--decode-sk", "65536", "--steps", "3", "--warmup", "1",
+                    "--gpus", "2")
+    assert out["n_gpus"] == 2 and out["vs_single_gpu"]["within_tolerance"], out

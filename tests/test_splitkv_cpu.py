@@ -95,3 +95,54 @@ def test_oracle_combine_handles_empty_parts():
     assert np.all(oc[0, 0] == 0) and np.isneginf(lc[0, 0, 0])
     np.testing.assert_allclose(oc[0, 1:], 1.5)
     np.testing.assert_allclose(lc[0, 0, 1:], [np.log(2.0), 1.0 + np.log(2.0)])
+
+
+def _decode_rank_main(rank, world, port, result):
+    """Decode layout: one contiguous key chunk per rank, all query rows; every
+    rank combines every peer's partial for all rows (the all_gather stands in
+    for the NVLink peer reads of DecodeSplitKV)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        b, h, sq, sk = 1, 2, 16, 1000
+        q, k, v = R.inputs(b, h, sq, sk, "normal", seed=23)
+        kb, ke = S.contiguous_chunk(sk, world, rank)
+        if ke > kb:
+            o_p, l_p = R.emulate(q, k, v, False, kv_begin=kb, kv_end=ke)
+        else:
+            o_p, l_p = np.zeros((b, sq, h, 128)), np.full((b, h, sq), -np.inf)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (o_p.astype(np.float32), l_p.astype(np.float32)))
+        o, lse = R.combine([g[0] for g in gathered], [g[1] for g in gathered])
+        ref, ref_lse = R.reference(q, k, v, False)
+        result.put((rank, R.errors(o.transpose(0, 2, 1, 3), lse, ref, ref_lse)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_decode_split_kv_cpu_ranks_match_reference(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decode_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = sorted(q.get(timeout=10) for _ in range(world))
+    assert [r for r, _ in got] == list(range(world))
+    assert all(stats["max_abs"] < 2e-2 for _, stats in got)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_contiguous_chunks_cover(world):
+    for sk in (1, 100, 128, 1000, 131072):
+        ch = [S.contiguous_chunk(sk, world, r) for r in range(world)]
+        assert ch[0][0] == 0 and ch[-1][1] == sk
+        assert all(a[1] == b[0] for a, b in zip(ch, ch[1:]))
+        assert all(b % 128 == 0 or b == sk for b, _ in ch)
+        sizes = [e - b for b, e in ch]
+        assert max(sizes) - min(sizes) <= 128 * ((sk + 127) // 128 // world + 1)
