@@ -1,0 +1,421 @@
+// BF16 attention backward for B200 (sm_100a), BSHD layout, head dim 128.
+//
+// The reference implements only the forward pass (README.md:24). These
+// kernels compute dQ, dK, dV of O = softmax(Q K^T * scale) V (top-left causal
+// or dense) from Q, K, V, O, dO and the forward's LSE, with the standard
+// recomputation formulas (no attention matrix in HBM, no atomics, results
+// deterministic):
+//
+//   P = exp(S - LSE), S = scale Q K^T     D = rowsum(dO * O)   (preprocess)
+//   dV = P^T dO     dP = dO V^T     dS = P * (dP - D)
+//   dK = scale dS^T Q                   dQ = scale dS K
+//
+// One kernel template, two modes:
+//   KV mode: a work tile is (batch, head, 128 keys); K_j and V_j stay in
+//            shared memory while the loop runs over the query tiles i that
+//            see them: S^T = K_j Q_i^T and dP^T = V_j dO_i^T (TMEM), then per
+//            key (TMEM lane) P^T and dS^T, then dV += P^T dO_i and
+//            dK += dS^T Q_i, accumulated in TMEM for the whole loop.
+//   Q mode:  a work tile is (batch, head, 128 query rows); Q_i and dO_i stay,
+//            the loop runs over the key tiles j: S, dP, dS per row, then
+//            dQ += dS K_j.
+// Every MMA form is the forward's: A and B K-major in shared memory for S and
+// dP, A (P^T, dS^T or dS as BF16 pairs) from TMEM with B MN-major for the
+// accumulations.
+//
+//   warps 0-3  elementwise: one TMEM lane per thread, 32 columns at a time
+//   warp 4     TMA: the outer tile pair once per work tile, then a ring of two
+//              stages of the inner tile pair
+//   warp 5     one thread issues every MMA and allocates TMEM
+//
+// TMEM (512 columns): T0 S^T / S, T1 dP^T / dP (their first 64 columns are
+// overwritten by P^T and dS^T / dS), T2 dV / dQ, T3 dK.
+#pragma once
+#include "attn_fwd_sm100.cuh"
+
+namespace fav4 {
+
+struct BwdParams {
+  const float* lse;   // forward LSE [B, H, Sq] (natural log)
+  const float* dsum;  // D = rowsum(dO * O) [B, H, Sq]
+  __nv_bfloat16* g0;  // KV mode: dK, Q mode: dQ  ([B, S, H, 128])
+  __nv_bfloat16* g1;  // KV mode: dV
+  int batch, heads, sq, sk;
+  float scale;        // softmax scale
+  float scale_log2;   // scale * log2(e)
+  int num_outer;      // outer tiles per (batch, head)
+  int num_tiles;      // batch * heads * num_outer
+  uint32_t* status;
+  uint64_t wait_limit_ns;
+};
+
+struct BwdSmem {
+  static constexpr int kOuter = 0;                   // 2 x 32 KiB
+  static constexpr int kInner = 2 * kTileBytes;      // 2 stages x 2 x 32 KiB
+  static constexpr int kBar = kInner + 4 * kTileBytes;
+  static constexpr int kOuterFull = 0, kOuterEmpty = 1, kInFull = 2, kInEmpty = 4;
+  static constexpr int kSFull = 6, kPFull = 7, kAccFull = 8, kAccEmpty = 9, kTeardown = 10;
+  static constexpr int kNumBars = 11;
+  static constexpr int kTmemHolder = kBar + kNumBars * 8;
+  static constexpr int kAbort = kTmemHolder + 4;
+  static constexpr int kBytes = kAbort + 4;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kAlloc <= 227 * 1024, "shared memory budget");
+};
+
+// Inner-loop range of a work tile: KV mode, query tiles [lo, hi) that see keys
+// [o0, o0+128); Q mode, key tiles [lo, hi) that rows [o0, o0+128) see.
+template <bool KV, bool Causal>
+__device__ __forceinline__ void bwd_range(const BwdParams& p, int o0, int& lo, int& hi) {
+  const int nq = (p.sq + kBlockM - 1) / kBlockM, nk = (p.sk + kBlockN - 1) / kBlockN;
+  if (KV) {
+    lo = Causal ? o0 / kBlockM : 0;  // a query row r sees key c iff c <= r
+    hi = (o0 < p.sk && (!Causal || o0 < p.sq)) ? nq : lo;
+  } else {
+    lo = 0;
+    hi = o0 < p.sq ? (Causal ? min(nk, o0 / kBlockN + 1) : nk) : 0;
+  }
+}
+
+template <bool Causal>
+__device__ __forceinline__ void bwd_tile(const BwdParams& p, int t, int& b, int& h, int& idx, bool kv) {
+  const int per_batch = p.heads * p.num_outer;
+  b = t / per_batch;
+  const int w = t - b * per_batch;
+  h = w % p.heads;
+  const int k = w / p.heads;
+  // causal: the longest loops first (low key tiles in KV mode, high row tiles in Q mode)
+  idx = (Causal && !kv) ? p.num_outer - 1 - k : k;
+}
+
+template <bool KV, bool Causal>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_o0, const __grid_constant__ CUtensorMap tm_o1,
+                          const __grid_constant__ CUtensorMap tm_i0, const __grid_constant__ CUtensorMap tm_i1,
+                          const BwdParams p) {
+  using L = BwdSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + L::kBar;
+  auto bar = [&](int slot) -> uint32_t { return bar0 + 8u * slot; };
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kAbort);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kTmemHolder);
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  WaitCtl ctl{abort_flag, p.status, p.wait_limit_ns};
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0u;
+    mbar_init(bar(L::kOuterFull), 1);
+    mbar_init(bar(L::kOuterEmpty), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(L::kInFull + s), 1);
+      mbar_init(bar(L::kInEmpty + s), 1);
+    }
+    mbar_init(bar(L::kSFull), 1);
+    mbar_init(bar(L::kPFull), 4);     // elementwise warps
+    mbar_init(bar(L::kAccFull), 1);
+    mbar_init(bar(L::kAccEmpty), 4);  // elementwise warps, after the epilogue read
+    mbar_init(bar(L::kTeardown), 1);
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tm_o0);
+    tma_prefetch_desc(&tm_o1);
+    tma_prefetch_desc(&tm_i0);
+    tma_prefetch_desc(&tm_i1);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_addr(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 4) {
+    // ============================ TMA producer ============================
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();
+      Ring ring;
+      uint32_t outer_empty_par = 1;
+      uint32_t armed = 0, armed_par = 0;  // inner stages (bits 0-1) and the outer pair (bit 2) in flight
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, h, idx, lo, hi;
+        bwd_tile<Causal>(p, t, b, h, idx, KV);
+        const int o0 = idx * kBlockM;
+        bwd_range<KV, Causal>(p, o0, lo, hi);
+        if (hi <= lo) continue;
+        if (!mbar_wait(bar(L::kOuterEmpty), outer_empty_par, ctl, kStatusTimeoutLoad)) { ok = false; break; }
+        outer_empty_par ^= 1u;
+        mbar_arrive_expect_tx(bar(L::kOuterFull), 2 * kTileBytes);
+        armed |= 4u;
+        armed_par = (armed_par & ~4u) | (outer_empty_par << 2);  // parity of this fill
+        for (int c = 0; c < 2; ++c) {
+          tma_load_4d(sbase + L::kOuter + c * kBoxBytes, &tm_o0, bar(L::kOuterFull), c * 64, h, o0, b, pol);
+          tma_load_4d(sbase + L::kOuter + kTileBytes + c * kBoxBytes, &tm_o1, bar(L::kOuterFull), c * 64, h, o0, b,
+                      pol);
+        }
+        for (int n = lo; n < hi && ok; ++n) {
+          if (!mbar_wait(bar(L::kInEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar(L::kInFull + ring.stage);
+          mbar_arrive_expect_tx(fb, 2 * kTileBytes);
+          armed |= 1u << ring.stage;
+          armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
+          const uint32_t dst = sbase + L::kInner + ring.stage * 2 * kTileBytes;
+          const int row = n * kBlockM;
+          for (int c = 0; c < 2; ++c) {
+            tma_load_4d(dst + c * kBoxBytes, &tm_i0, fb, c * 64, h, row, b, pol);
+            tma_load_4d(dst + kTileBytes + c * kBoxBytes, &tm_i1, fb, c * 64, h, row, b, pol);
+          }
+          ring.advance<2>();
+        }
+      }
+      if (!ok) {
+        // Let every copy this thread issued land before the CTA exits.
+        WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
+        volatile uint32_t no_abort = 0;
+        drain.abort = &no_abort;
+        for (int s = 0; s < 2; ++s)
+          if (armed & (1u << s)) mbar_wait(bar(L::kInFull + s), (armed_par >> s) & 1u, drain, kStatusTimeoutDrain);
+        if (armed & 4u) mbar_wait(bar(L::kOuterFull), (armed_par >> 2) & 1u, drain, kStatusTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ============================= MMA issuer =============================
+    if (lane == 0) {
+      constexpr uint32_t idesc_ss = make_idesc_bf16(kBlockM, kBlockN, false);
+      constexpr uint32_t idesc_ts = make_idesc_bf16(kBlockM, kHeadDim, true);
+      const uint64_t dk = make_sdesc_sw128(sbase, 16, 1024);
+      const uint64_t dv = make_sdesc_sw128(sbase, kBoxBytes, 1024);
+      const uint32_t k_lo = static_cast<uint32_t>(dk), k_hi = static_cast<uint32_t>(dk >> 32);
+      const uint32_t v_lo = static_cast<uint32_t>(dv), v_hi = static_cast<uint32_t>(dv >> 32);
+      Ring ring;
+      uint32_t outer_full_par = 0, p_par = 0, acc_empty_par = 1;
+      bool ok = true;
+      // D (tmem column d) = A (shared tile a) * B (shared tile bt)^T, both K-major
+      auto mma_ss = [&](uint32_t d, int a_off, int b_off) {
+        const uint32_t aa = k_lo + (a_off >> 4), ba = k_lo + (b_off >> 4);
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k) {
+          const uint32_t off = ((k / 4) * kBoxBytes + (k % 4) * 32) >> 4;
+          umma_ss_w(tmem + d, aa + off, k_hi, ba + off, k_hi, idesc_ss, k > 0 ? 1u : 0u);
+        }
+      };
+      // D (tmem column d) (+)= A (tmem column a, BF16 pairs) * B (shared tile b, MN-major)
+      auto mma_ts = [&](uint32_t d, uint32_t a, int b_off, bool acc) {
+        const uint32_t ba = v_lo + (b_off >> 4);
+#pragma unroll
+        for (int k = 0; k < kBlockN / 16; ++k)
+          umma_ts_w(tmem + d, tmem + a + k * 8, ba + ((k * 2048) >> 4), v_hi, idesc_ts, (acc || k > 0) ? 1u : 0u);
+      };
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, h, idx, lo, hi;
+        bwd_tile<Causal>(p, t, b, h, idx, KV);
+        bwd_range<KV, Causal>(p, idx * kBlockM, lo, hi);
+        if (hi <= lo) continue;
+        if (!mbar_wait(bar(L::kOuterFull), outer_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
+        outer_full_par ^= 1u;
+        if (!mbar_wait(bar(L::kAccEmpty), acc_empty_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
+        acc_empty_par ^= 1u;
+        for (int n = lo; n < hi && ok; ++n) {
+          if (!mbar_wait(bar(L::kInFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const int in0 = L::kInner + ring.stage * 2 * kTileBytes, in1 = in0 + kTileBytes;
+          mma_ss(0, L::kOuter, in0);                // T0 = outer0 inner0^T
+          mma_ss(128, L::kOuter + kTileBytes, in1);  // T1 = outer1 inner1^T
+          tc_commit(bar(L::kSFull));
+          if (!mbar_wait(bar(L::kPFull), p_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
+          p_par ^= 1u;
+          tc_fence_after();
+          if (KV) {
+            mma_ts(256, 0, in1, n > lo);    // dV += P^T dO_i
+            mma_ts(384, 128, in0, n > lo);  // dK += dS^T Q_i
+          } else {
+            mma_ts(256, 128, in0, n > lo);  // dQ += dS K_j
+          }
+          tc_commit(bar(L::kInEmpty + ring.stage));
+          ring.advance<2>();
+        }
+        if (!ok) break;
+        tc_commit(bar(L::kOuterEmpty));
+        tc_commit(bar(L::kAccFull));
+      }
+      tc_commit(bar(L::kTeardown));
+      WaitCtl drain{abort_flag, p.status, p.wait_limit_ns};
+      volatile uint32_t no_abort = 0;
+      drain.abort = &no_abort;
+      mbar_wait(bar(L::kTeardown), 0, drain, kStatusTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ============================ elementwise =============================
+    const int row = warp * 32 + lane;  // TMEM lane: a key (KV mode) or a query row (Q mode)
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const float log2e = 1.4426950408889634f;
+    uint32_t s_par = 0, acc_full_par = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      int b, h, idx, lo, hi;
+      bwd_tile<Causal>(p, t, b, h, idx, KV);
+      const int o0 = idx * kBlockM;
+      bwd_range<KV, Causal>(p, o0, lo, hi);
+      const int mine = o0 + row;  // this thread's key (KV) or query row (Q)
+      const int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.sq;  // LSE / D row base
+      // Q mode: this row's statistics (rows past Sq read row Sq-1 and are not stored)
+      float lse2_row = 0.f, d_row = 0.f;
+      if (!KV) {
+        const int r = min(mine, p.sq - 1);
+        lse2_row = p.lse[stat0 + r] * log2e;
+        d_row = p.dsum[stat0 + r];
+      }
+      for (int n = lo; n < hi; ++n) {
+        if (!warp_wait(bar(L::kSFull), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+        s_par ^= 1u;
+        tc_fence_after();
+        const int c0 = n * kBlockN;  // first column: a query row (KV) or a key (Q)
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tmem + lane_off + ch * 32, sr);
+          tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
+          tmem_ld_wait();
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int col = c0 + ch * 32 + c + e;
+              int r, key;
+              float lse2, dd;
+              if (KV) {
+                r = col;
+                key = mine;
+                const int rc = min(r, p.sq - 1);
+                lse2 = p.lse[stat0 + rc] * log2e;
+                dd = p.dsum[stat0 + rc];
+              } else {
+                r = mine;
+                key = col;
+                lse2 = lse2_row;
+                dd = d_row;
+              }
+              const bool valid = r < p.sq && key < p.sk && (!Causal || key <= r);
+              const float s = __uint_as_float(sr[c + e]);
+              const float pr = valid ? ex2_mufu(s * p.scale_log2 - lse2) : 0.f;
+              pv[e] = pr;
+              dsv[e] = pr * (__uint_as_float(dr[c + e]) - dd);
+            }
+            pk[c / 2] = pack_bf16x2(pv[0], pv[1]);
+            dk[c / 2] = pack_bf16x2(dsv[0], dsv[1]);
+          }
+          // column chunk ch of P^T / dS^T (BF16 pairs) lands in columns [16 ch, 16 ch + 16),
+          // S / dP columns this thread has already read
+          if (KV) tmem_st16(tmem + lane_off + ch * 16, pk);
+          tmem_st16(tmem + lane_off + 128 + ch * 16, dk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::kPFull));
+      }
+      if (!ok) break;
+      // ------------------------------ epilogue ------------------------------
+      if (hi <= lo) {
+        // nothing attends this tile (KV mode: keys no query row sees): zero gradients
+        if (KV && mine < p.sk) {
+          const int64_t off = ((static_cast<int64_t>(b) * p.sk + mine) * p.heads + h) * kHeadDim;
+          uint4* d0 = reinterpret_cast<uint4*>(p.g0 + off);
+          uint4* d1 = reinterpret_cast<uint4*>(p.g1 + off);
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            d0[v] = make_uint4(0u, 0u, 0u, 0u);
+            d1[v] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        continue;
+      }
+      if (!warp_wait(bar(L::kAccFull), acc_full_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+      acc_full_par ^= 1u;
+      tc_fence_after();
+      const int limit = KV ? p.sk : p.sq;
+      const int64_t off = ((static_cast<int64_t>(b) * limit + mine) * p.heads + h) * kHeadDim;
+#pragma unroll 1
+      for (int g = 0; g < (KV ? 2 : 1); ++g) {
+        // KV: g = 0 dK (column 384, times scale), g = 1 dV (column 256); Q: dQ (column 256, times scale)
+        const uint32_t col = KV ? (g == 0 ? 384u : 256u) : 256u;
+        const float mul = (KV && g == 1) ? 1.f : p.scale;
+        __nv_bfloat16* dst_row = (g == 0 ? p.g0 : p.g1) + off;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t acc[32];
+          tmem_ld32(tmem + lane_off + col + ch * 32, acc);
+          tmem_ld_wait();
+          if (mine < limit) {
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + ch * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(acc[8 * v + 0]) * mul, __uint_as_float(acc[8 * v + 1]) * mul);
+              w.y = pack_bf16x2(__uint_as_float(acc[8 * v + 2]) * mul, __uint_as_float(acc[8 * v + 3]) * mul);
+              w.z = pack_bf16x2(__uint_as_float(acc[8 * v + 4]) * mul, __uint_as_float(acc[8 * v + 5]) * mul);
+              w.w = pack_bf16x2(__uint_as_float(acc[8 * v + 6]) * mul, __uint_as_float(acc[8 * v + 7]) * mul);
+              dst[v] = w;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::kAccEmpty));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// D = rowsum(dO * O) in FP32, one warp per (batch, row, head).
+__global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o,
+                                                            const __nv_bfloat16* __restrict__ dout,
+                                                            float* __restrict__ dsum, int batch, int sq, int heads) {
+  const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
+  const int lane = threadIdx.x % 32;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < rows;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const uint2 a = reinterpret_cast<const uint2*>(o + w * kHeadDim)[lane];
+    const uint2 g = reinterpret_cast<const uint2*>(dout + w * kHeadDim)[lane];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
+      s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    if (lane == 0) {
+      // w = (b * sq + r) * heads + h  ->  D[b, h, r]
+      const int h = static_cast<int>(w % heads);
+      const int64_t br = w / heads;
+      const int r = static_cast<int>(br % sq);
+      const int64_t bb = br / sq;
+      dsum[(bb * heads + h) * sq + r] = s;
+    }
+  }
+}
+
+}  // namespace fav4

@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "attn_fwd_sm100.cuh"
+#include "attn_bwd_sm100.cuh"
 #include "combine.cuh"
 #include "tensor_map.h"
 #include "fav4_bshd.h"
@@ -543,6 +544,115 @@ extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, 
   if (config == 0) config = fav4_bshd_select_config(a);
   if (splits == 1) return fav4_bshd_forward_partial(a, causal, config, kv_begin, kv_end, stream);
   return fav4::splitkv_range(a, causal, config, kv_begin, kv_end, splits, workspace, workspace_bytes, stream);
+}
+
+// --------------------------------------------------------------------------
+// Backward pass (no reference counterpart): D = rowsum(dO * O), then the KV
+// kernel (dK, dV) and the Q kernel (dQ), all on the caller's stream.
+namespace fav4 {
+namespace {
+
+bool bwd_args_valid(const Fav4BwdArgs* a, int causal) {
+  if (!a || !a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
+      a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->sk <= 0 || (causal != 0 && causal != 1) ||
+      !std::isfinite(a->scale) || a->scale <= 0)
+    return false;
+  if (a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128) ||
+      a->sk > INT_MAX / (a->heads * 128))
+    return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                       reinterpret_cast<uintptr_t>(a->v) | reinterpret_cast<uintptr_t>(a->o) |
+                       reinterpret_cast<uintptr_t>(a->dout) | reinterpret_cast<uintptr_t>(a->dq) |
+                       reinterpret_cast<uintptr_t>(a->dk) | reinterpret_cast<uintptr_t>(a->dv);
+  return (al & 15) == 0 && (reinterpret_cast<uintptr_t>(a->lse) & 3) == 0;
+}
+
+template <bool KV, bool Causal>
+int launch_bwd(const BwdParams& base, const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& i0,
+               const CUtensorMap& i1, int outer_len, const DeviceInfo& info, int dev, cudaStream_t stream) {
+  auto kernel = attn_bwd_sm100_kernel<KV, Causal>;
+  constexpr int smem = BwdSmem::kAlloc;
+  {
+    static std::mutex mu;
+    static bool attr_set[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  BwdParams p = base;
+  p.num_outer = (outer_len + kBlockM - 1) / kBlockM;
+  const int64_t tiles = static_cast<int64_t>(p.batch) * p.heads * p.num_outer;
+  if (tiles > INT_MAX) return cudaErrorInvalidValue;
+  p.num_tiles = static_cast<int>(tiles);
+  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  kernel<<<grid, 192, smem, stream>>>(o0, o1, i0, i1, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* a) {
+  if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->batch > INT_MAX / a->heads ||
+      a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128))
+    return 0;
+  return fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4);
+}
+
+extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream) {
+  if (!fav4::bwd_args_valid(a, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < fav4_bshd_backward_workspace_bytes(a))
+    return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  fav4::DeviceInfo info;
+  if (!fav4::device_info(dev, &info)) return cudaErrorInvalidDevice;
+  CUtensorMap tq, tk, tv, tdo;
+  if (!fav4::encode_bshd(&tq, a->q, a->batch, a->sq, a->heads) ||
+      !fav4::encode_bshd(&tk, a->k, a->batch, a->sk, a->heads) ||
+      !fav4::encode_bshd(&tv, a->v, a->batch, a->sk, a->heads) ||
+      !fav4::encode_bshd(&tdo, a->dout, a->batch, a->sq, a->heads))
+    return cudaErrorInvalidValue;
+  float* dsum = static_cast<float*>(workspace);
+  {
+    const int64_t rows = static_cast<int64_t>(a->batch) * a->sq * a->heads;
+    const int64_t want = (rows + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(info.sms) * 16;
+    fav4::attn_bwd_dsum_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), dsum, a->batch, a->sq,
+        a->heads);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  fav4::BwdParams p = {};
+  p.lse = a->lse;
+  p.dsum = dsum;
+  p.batch = a->batch;
+  p.heads = a->heads;
+  p.sq = a->sq;
+  p.sk = a->sk;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.status = info.status;
+  p.wait_limit_ns = fav4::wait_limit_ns();
+  // KV kernel: dK, dV
+  fav4::BwdParams pk = p;
+  pk.g0 = static_cast<__nv_bfloat16*>(a->dk);
+  pk.g1 = static_cast<__nv_bfloat16*>(a->dv);
+  e = static_cast<cudaError_t>(causal ? fav4::launch_bwd<true, true>(pk, tk, tv, tq, tdo, a->sk, info, dev, stream)
+                                      : fav4::launch_bwd<true, false>(pk, tk, tv, tq, tdo, a->sk, info, dev, stream));
+  if (e != cudaSuccess) return e;
+  // Q kernel: dQ
+  fav4::BwdParams pq = p;
+  pq.g0 = static_cast<__nv_bfloat16*>(a->dq);
+  pq.g1 = nullptr;
+  return causal ? fav4::launch_bwd<false, true>(pq, tq, tdo, tk, tv, a->sq, info, dev, stream)
+                : fav4::launch_bwd<false, false>(pq, tq, tdo, tk, tv, a->sq, info, dev, stream);
 }
 
 extern "C" int fav4_bshd_pipeline_status(int clear) {

@@ -28,6 +28,13 @@ class Args(C.Structure):
         (n, C.c_int) for n in ("batch", "heads", "sq", "sk")] + [("scale", C.c_float)]
 
 
+class BwdArgs(C.Structure):
+    """Fav4BwdArgs (include/fav4_bshd.h): arguments of fav4_bshd_backward."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "dout", "lse", "dq", "dk", "dv")] + [
+        (n, C.c_int) for n in ("batch", "heads", "sq", "sk")] + [("scale", C.c_float)]
+
+
 class HostOut(C.Structure):
     """Fav4HostOut (include/fav4_bshd.h): one output of fav4_bshd_forward_host."""
 
@@ -67,6 +74,10 @@ def _bind(lib):
     lib.fav4_bshd_forward_host.argtypes = [C.POINTER(Args), C.POINTER(HostOut), C.c_int, C.c_int, C.c_void_p,
                                            C.c_size_t, C.c_void_p]
     lib.fav4_bshd_forward_host.restype = C.c_int
+    lib.fav4_bshd_backward_workspace_bytes.argtypes = [C.POINTER(BwdArgs)]
+    lib.fav4_bshd_backward_workspace_bytes.restype = C.c_size_t
+    lib.fav4_bshd_backward.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.fav4_bshd_backward.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
     lib.fav4_bshd_pipeline_status.restype = C.c_int
     return lib
@@ -255,6 +266,27 @@ class Runner:
         if status:
             raise RuntimeError(f"forward_host: CUDA status {status}")
 
+    def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None):
+        """dQ, dK, dV through fav4_bshd_backward (all BF16 BSHD CUDA tensors,
+        lse the forward's FP32 [B, H, Sq]). The D workspace is allocated with
+        torch and kept for the next call of the same shape."""
+        import torch
+        for x in (q, k, v, o, dout, dq, dk, dv):
+            assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
+        b, sq, h, d = q.shape
+        assert d == HEAD_DIM and k.shape == v.shape == dk.shape == dv.shape and k.shape[0] == b and k.shape[2] == h
+        assert o.shape == dout.shape == dq.shape == q.shape
+        assert lse.shape == (b, h, sq) and lse.dtype == torch.float32 and lse.is_contiguous()
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        a = BwdArgs(*(x.data_ptr() for x in (q, k, v, o, dout, lse, dq, dk, dv)), b, h, sq, k.shape[1], scale)
+        need = self.lib.fav4_bshd_backward_workspace_bytes(C.byref(a))
+        ws = getattr(self, "_bwd_ws", None)
+        if ws is None or ws.numel() < need or ws.device != q.device:
+            ws = self._bwd_ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+        status = self.lib.fav4_bshd_backward(C.byref(a), int(causal), ws.data_ptr(), ws.numel(), _stream(stream))
+        if status:
+            raise RuntimeError(f"backward: CUDA status {status}")
+
     def select_config(self, q, k, v, o, lse=None):
         a = self.args(q, k, v, o, lse)
         return self.lib.fav4_bshd_select_config(C.byref(a))
@@ -273,5 +305,5 @@ def forward(q, k, v, causal=False, config=0, scale=None, return_lse=False, out=N
     return (o, lse) if return_lse else o
 
 
-__all__ = ["Args", "HostOut", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
+__all__ = ["Args", "BwdArgs", "HostOut", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
            "HEAD_DIM", "CUDA_ERROR_INVALID_VALUE"]

@@ -133,6 +133,34 @@ size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* args, int splits);
  * error. */
 int fav4_bshd_splitkv_splits(const Fav4Args* args, int causal, int config);
 
+/* Backward pass (no reference counterpart: the reference implements the
+ * forward only, README.md:24). Tensors BF16 [batch, seq, heads, 128],
+ * contiguous, 16-byte aligned: q, k, v and the forward's o; dout = dL/dO; lse
+ * = the forward's LSE (FP32 [batch, heads, sq], from fav4_bshd_forward with
+ * a non-NULL lse). Writes dq, dk, dv (same layouts as q, k, v). */
+struct Fav4BwdArgs {
+  const void *q, *k, *v, *o, *dout;
+  const float* lse;
+  void *dq, *dk, *dv;
+  int batch, heads, sq, sk;
+  float scale;
+};
+typedef struct Fav4BwdArgs Fav4BwdArgs;
+
+/* Device workspace fav4_bshd_backward needs (D = rowsum(dO * O), FP32
+ * [batch, heads, sq]); 0 on invalid arguments. */
+size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* args);
+
+/* dQ, dK, dV of O = softmax(Q K^T * scale) V (causal: top-left). Three
+ * kernels on `stream`: D, then dK/dV (work tiles of 128 keys), then dQ (work
+ * tiles of 128 query rows); no atomics, deterministic. Same mask convention
+ * as fav4_bshd_forward; keys no query row sees get zero gradients. workspace:
+ * device memory, 256-byte aligned, fav4_bshd_backward_workspace_bytes long.
+ * Returns 0, cudaErrorInvalidValue (1) on invalid arguments, else the first
+ * failing launch status. */
+int fav4_bshd_backward(const Fav4BwdArgs* args, int causal, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
 /* One output of fav4_bshd_forward_host: host buffers for O (BF16
  * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and
  * the mask and config it is computed with. */

@@ -20,6 +20,9 @@ Contents, each restating the reference (rocking5566/flash-attention-v4-rocm):
 * ``combine``: the LSE-weighted merge of split-KV partials that the library's
   combine kernel computes (the reference has no split-KV path; this is the
   checker for it).
+* ``reference_backward``: FP64 gradients dQ, dK, dV of the same attention
+  (the reference has no backward pass, README.md:24; this is the checker for
+  the library's). Pinned on the CPU against torch autograd of the same math.
 * ``emulate``: a kernel-faithful FP32 emulation (tiles of 128 keys, lazy
   rescale with threshold 8 base-2 units, P rounded to BF16, row sum over the
   unrounded FP32 probabilities: src/bshd_kernel.hpp:148-181) that explains the
@@ -170,6 +173,36 @@ def reference(q, k, v, causal: bool, rows=None, scale: float | None = None):
     vs = np.ascontiguousarray(v.transpose(0, 2, 1, 3), dtype=np.float64)
     o = (e / ssum) @ vs
     return o, lse
+
+
+def reference_backward(q, k, v, do, causal: bool, scale: float | None = None):
+    """FP64 gradients of O = softmax(Q K^T * scale) V (top-left causal) with
+    respect to Q, K, V for the output gradient dO. Arrays [B,S,H,128]; returns
+    dQ, dK, dV in the same layout, plus the forward O [B,S,H,128] and LSE
+    [B,H,Sq] the backward consumes. Standard formulas: P = exp(S - LSE),
+    dV = P^T dO, dP = dO V^T, D = rowsum(dO * O), dS = P * (dP - D),
+    dQ = scale * dS K, dK = scale * dS^T Q."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qs, ks, vs, dos = (np.ascontiguousarray(x.transpose(0, 2, 1, 3), dtype=np.float64) for x in (q, k, v, do))
+    s_ = (qs @ ks.transpose(0, 1, 3, 2)) * scale
+    if causal:
+        mask = np.arange(k.shape[1])[None, :] > np.arange(q.shape[1])[:, None]
+        s_[:, :, mask] = -np.inf
+    mx = s_.max(-1, keepdims=True)
+    e = np.exp(s_ - mx)
+    ssum = e.sum(-1, keepdims=True)
+    p_ = e / ssum
+    lse = (np.log(ssum) + mx)[..., 0]
+    o = p_ @ vs
+    dv = p_.transpose(0, 1, 3, 2) @ dos
+    dp = dos @ vs.transpose(0, 1, 3, 2)
+    dd = (dos * o).sum(-1, keepdims=True)
+    ds = p_ * (dp - dd)
+    dq = scale * (ds @ ks)
+    dk = scale * (ds.transpose(0, 1, 3, 2) @ qs)
+    back = lambda x: x.transpose(0, 2, 1, 3)  # noqa: E731
+    return back(dq), back(dk), back(dv), back(o), lse
 
 
 def reference_chunked(q, k, v, causal: bool, rows, scale: float | None = None, max_elems: int = 1 << 26):

@@ -212,3 +212,25 @@ def test_splitkv_rejects_invalid_arguments(lib):
     assert f(C.byref(a), 2, 0, 4, ws, need, None) == INVALID          # bad mode
     b = make_args(q=None)
     assert f(C.byref(b), 0, 0, 4, ws, need, None) == INVALID
+
+
+def test_backward_rejects_invalid_arguments(lib):
+    def bwd(**kw):
+        a = dict(q=A16, k=A16 * 2, v=A16 * 3, o=A16 * 4, dout=A16 * 5, lse=A16 * 6, dq=A16 * 7, dk=A16 * 8,
+                 dv=A16 * 9, batch=2, heads=4, sq=64, sk=80, scale=0.1)
+        a.update(kw)
+        return F.BwdArgs(*(a[n] for n in ("q", "k", "v", "o", "dout", "lse", "dq", "dk", "dv")), a["batch"],
+                         a["heads"], a["sq"], a["sk"], a["scale"])
+    good = bwd()
+    need = lib.fav4_bshd_backward_workspace_bytes(C.byref(good))
+    assert need == (2 * 4 * 64 * 4 + 255) // 256 * 256
+    ws = A16 * 256
+    f = lib.fav4_bshd_backward
+    for kw in (dict(q=None), dict(dout=None), dict(lse=None), dict(dk=None), dict(batch=0), dict(sk=0),
+               dict(scale=0.0), dict(scale=float("nan")), dict(dq=A16 + 8), dict(lse=A16 + 2),
+               dict(heads=2 ** 24 + 1)):
+        assert f(C.byref(bwd(**kw)), 0, ws, need, None) == INVALID, kw
+    assert f(C.byref(good), 2, ws, need, None) == INVALID        # bad mode
+    assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
+    assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
+    assert f(C.byref(good), 0, None, need, None) == INVALID

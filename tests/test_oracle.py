@@ -123,3 +123,24 @@ def test_grouped_query_reference_is_repeated_kv():
         assert np.array_equal(o, o2) and np.array_equal(lse, lse2)
         oc, lc = R.reference_chunked(q, k, v, causal, np.arange(40), max_elems=512)
         np.testing.assert_allclose(oc, o, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_reference_backward_matches_torch_autograd(causal):
+    """The oracle's FP64 gradients equal torch autograd of the same FP64 math."""
+    import torch
+    q, k, v = R.inputs(2, 3, 70, 90, "normal", seed=12)
+    do = R.inputs(2, 3, 70, 70, "normal", seed=13)[0]
+    scale = 0.1
+    dq, dk, dv, o, lse = R.reference_backward(q, k, v, do, causal, scale)
+    tq, tk, tv = (torch.tensor(x.transpose(0, 2, 1, 3), dtype=torch.float64, requires_grad=True) for x in (q, k, v))
+    s = tq @ tk.transpose(-1, -2) * scale
+    if causal:
+        s = s.masked_fill(torch.ones(70, 90, dtype=torch.bool).triu(1), float("-inf"))
+    to = torch.softmax(s, -1) @ tv
+    to.backward(torch.tensor(do.transpose(0, 2, 1, 3), dtype=torch.float64))
+    for mine, theirs in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad), (o, to.detach())):
+        np.testing.assert_allclose(mine.transpose(0, 2, 1, 3), theirs.numpy(), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(lse, torch.logsumexp(s, -1).detach().numpy(), rtol=1e-12, atol=1e-12)
+    ref_o, ref_lse = R.reference(q, k, v, causal, scale=scale)
+    np.testing.assert_allclose(o.transpose(0, 2, 1, 3), ref_o, rtol=1e-12, atol=1e-12)
