@@ -350,6 +350,59 @@ def run_compare(args):
         torch.cuda.empty_cache()
 
 
+def run_backward(args):
+    """Backward pass, one GPU: B H S of the headline (or --batch/--seq), dense
+    and causal. FLOPs by the usual convention, 2.5x the forward's (five
+    matmuls: dV, dP, dQ, dK and the recomputed S); this library computes seven
+    (S and dP in both the dK/dV and the dQ kernels). torch SDPA's cuDNN
+    backward on the same tensors is timed beside it. One JSON line per mask."""
+    import torch
+    import torch.nn.functional as Fn
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    import fav4_bshd
+    runner = fav4_bshd.Runner()
+    pk, pk_kind = peaks()
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v, do = (torch.randn((B, S, H, D), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(4))
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, S), device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    scale = 1 / math.sqrt(D)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    for causal in (False, True):
+        runner.call(q, k, v, o, lse, causal, 0, scale)
+        ms = timed(lambda: runner.backward(q, k, v, o, do, lse, dq, dk, dv, causal, scale))
+        f = 2.5 * flops(B, H, S, causal)
+        line = {"mode": "backward", "batch": B, "heads": H, "seq": S, "causal": causal, "ms": ms,
+                "tflops": f / (ms * 1e-3) / 1e12, "frac_of_measured_bf16": f / (ms * 1e-3) / 1e12 / pk["bf16_tflops"],
+                "peak_source": pk_kind, "flop_convention": "2.5 x forward (5 matmuls)",
+                "pipeline_status": runner.pipeline_status(clear=True)}
+        try:
+            tq, tk, tv = (x.transpose(1, 2).detach().requires_grad_(True) for x in (q, k, v))
+            tdo = do.transpose(1, 2)
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                out = Fn.scaled_dot_product_attention(tq, tk, tv, is_causal=causal, scale=scale)
+                cms = timed(lambda: torch.autograd.grad(out, (tq, tk, tv), tdo, retain_graph=True))
+            line["torch_sdpa_cudnn_ms"] = cms
+            line["torch_sdpa_cudnn_tflops"] = f / (cms * 1e-3) / 1e12
+        except Exception as e:  # noqa: BLE001
+            line["torch_sdpa_cudnn"] = f"unavailable: {type(e).__name__}: {str(e).splitlines()[0][:120]}"
+        emit(line)
+
+
 def run_decode(args):
     """Decode-like shapes on one GPU (few query rows against a long key cache):
     fav4_bshd_forward against the one-launch split-KV forward with the
@@ -536,6 +589,7 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="profiling only: per-GPU batch")
     ap.add_argument("--seq", type=int, default=S, help="profiling only: sequence length")
     ap.add_argument("--sweep", action="store_true", help="BASELINE configs[2] sequence sweep, one GPU")
+    ap.add_argument("--backward", action="store_true", help="backward pass timing (B/S of the headline or --batch/--seq)")
     ap.add_argument("--decode", action="store_true",
                     help="decode-like shapes (B1 H8, few query rows, long key cache): forward vs one-launch split-KV")
     ap.add_argument("--decode-sq", default="1,16,64,128")
@@ -553,6 +607,11 @@ def main():
         return
     if args.compare:
         run_compare(args)
+        return
+    if args.backward:
+        if (args.batch, args.seq) != (B, S):
+            set_shape(args.batch, args.seq)
+        run_backward(args)
         return
     if args.decode:
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:

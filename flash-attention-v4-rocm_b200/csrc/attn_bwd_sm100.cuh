@@ -36,7 +36,7 @@
 namespace fav4 {
 
 struct BwdParams {
-  const float* lse;   // forward LSE [B, H, Sq] (natural log)
+  const float* lse2;  // forward LSE * log2(e) [B, H, Sq] (written by the preprocess)
   const float* dsum;  // D = rowsum(dO * O) [B, H, Sq]
   __nv_bfloat16* g0;  // KV mode: dK, Q mode: dQ  ([B, S, H, 128])
   __nv_bfloat16* g1;  // KV mode: dV
@@ -259,9 +259,9 @@ __global__ void __launch_bounds__(192, 1)
     // ============================ elementwise =============================
     const int row = warp * 32 + lane;  // TMEM lane: a key (KV mode) or a query row (Q mode)
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const float log2e = 1.4426950408889634f;
     uint32_t s_par = 0, acc_full_par = 0;
     bool ok = true;
+    const float2 sc = make_float2(p.scale_log2, p.scale_log2);
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       int b, h, idx, lo, hi;
       bwd_tile<Causal>(p, t, b, h, idx, KV);
@@ -270,52 +270,69 @@ __global__ void __launch_bounds__(192, 1)
       const int mine = o0 + row;  // this thread's key (KV) or query row (Q)
       const int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.sq;  // LSE / D row base
       // Q mode: this row's statistics (rows past Sq read row Sq-1 and are not stored)
-      float lse2_row = 0.f, d_row = 0.f;
+      float2 lse2_row = make_float2(0.f, 0.f), d_row = make_float2(0.f, 0.f);
       if (!KV) {
         const int r = min(mine, p.sq - 1);
-        lse2_row = p.lse[stat0 + r] * log2e;
-        d_row = p.dsum[stat0 + r];
+        lse2_row.x = lse2_row.y = -p.lse2[stat0 + r];
+        d_row.x = d_row.y = -p.dsum[stat0 + r];
       }
       for (int n = lo; n < hi; ++n) {
         if (!warp_wait(bar(L::kSFull), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         s_par ^= 1u;
         tc_fence_after();
         const int c0 = n * kBlockN;  // first column: a query row (KV) or a key (Q)
+        // Masks only on boundary tiles: the causal diagonal and tails past Sq / Sk (rows and keys past
+        // the ends read zeros from TMA, which contribute nothing; the mask keeps exp2 finite there).
+        const int r_lo = KV ? c0 : o0, k_lo = KV ? o0 : c0;
+        const bool masked = (Causal && k_lo + kBlockN - 1 > r_lo) || r_lo + kBlockM > p.sq || k_lo + kBlockN > p.sk;
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t sr[32], dr[32];
           tmem_ld32(tmem + lane_off + ch * 32, sr);
           tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
+          // KV mode: the chunk's 32 query rows' statistics (the same for every lane), negated
+          float nl[32], nd[32];
+          if (KV) {
+            const int r0c = c0 + ch * 32;
+            if (r0c + 32 <= p.sq && ((stat0 + r0c) & 3) == 0) {  // whole chunk, 16-byte aligned
+              const float4* l4 = reinterpret_cast<const float4*>(p.lse2 + stat0 + r0c);
+              const float4* d4 = reinterpret_cast<const float4*>(p.dsum + stat0 + r0c);
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                const float4 x = l4[v], y = d4[v];
+                nl[4 * v] = -x.x, nl[4 * v + 1] = -x.y, nl[4 * v + 2] = -x.z, nl[4 * v + 3] = -x.w;
+                nd[4 * v] = -y.x, nd[4 * v + 1] = -y.y, nd[4 * v + 2] = -y.z, nd[4 * v + 3] = -y.w;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const int rc = min(r0c + c, p.sq - 1);
+                nl[c] = -p.lse2[stat0 + rc];
+                nd[c] = -p.dsum[stat0 + rc];
+              }
+            }
+          }
           tmem_ld_wait();
           uint32_t pk[16], dk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            float pv[2], dsv[2];
+            const float2 nl2 = KV ? make_float2(nl[c], nl[c + 1]) : lse2_row;
+            const float2 nd2 = KV ? make_float2(nd[c], nd[c + 1]) : d_row;
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc, nl2);
+            float2 pr = make_float2(ex2_mufu(x.x), ex2_mufu(x.y));
+            if (masked) {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int col = c0 + ch * 32 + c + e;
-              int r, key;
-              float lse2, dd;
-              if (KV) {
-                r = col;
-                key = mine;
-                const int rc = min(r, p.sq - 1);
-                lse2 = p.lse[stat0 + rc] * log2e;
-                dd = p.dsum[stat0 + rc];
-              } else {
-                r = mine;
-                key = col;
-                lse2 = lse2_row;
-                dd = d_row;
+              for (int e = 0; e < 2; ++e) {
+                const int col = c0 + ch * 32 + c + e;
+                const int r = KV ? col : mine, key = KV ? mine : col;
+                const bool valid = r < p.sq && key < p.sk && (!Causal || key <= r);
+                if (!valid) (e == 0 ? pr.x : pr.y) = 0.f;
               }
-              const bool valid = r < p.sq && key < p.sk && (!Causal || key <= r);
-              const float s = __uint_as_float(sr[c + e]);
-              const float pr = valid ? ex2_mufu(s * p.scale_log2 - lse2) : 0.f;
-              pv[e] = pr;
-              dsv[e] = pr * (__uint_as_float(dr[c + e]) - dd);
             }
-            pk[c / 2] = pack_bf16x2(pv[0], pv[1]);
-            dk[c / 2] = pack_bf16x2(dsv[0], dsv[1]);
+            const float2 dp = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), nd2);
+            const float2 ds = __fmul2_rn(pr, dp);
+            pk[c / 2] = pack_bf16x2(pr.x, pr.y);
+            dk[c / 2] = pack_bf16x2(ds.x, ds.y);
           }
           // column chunk ch of P^T / dS^T (BF16 pairs) lands in columns [16 ch, 16 ch + 16),
           // S / dP columns this thread has already read
@@ -387,10 +404,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// D = rowsum(dO * O) in FP32, one warp per (batch, row, head).
+// D = rowsum(dO * O) in FP32 and LSE * log2(e), one warp per (batch, row, head).
 __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o,
                                                             const __nv_bfloat16* __restrict__ dout,
-                                                            float* __restrict__ dsum, int batch, int sq, int heads) {
+                                                            const float* __restrict__ lse, float* __restrict__ dsum,
+                                                            float* __restrict__ lse2, int batch, int sq, int heads) {
   const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
   const int lane = threadIdx.x % 32;
   for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < rows;
@@ -413,7 +431,9 @@ __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16*
       const int64_t br = w / heads;
       const int r = static_cast<int>(br % sq);
       const int64_t bb = br / sq;
-      dsum[(bb * heads + h) * sq + r] = s;
+      const int64_t at = (bb * heads + h) * sq + r;
+      dsum[at] = s;
+      lse2[at] = lse[at] * 1.4426950408889634f;
     }
   }
 }

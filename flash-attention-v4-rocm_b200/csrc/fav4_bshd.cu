@@ -599,7 +599,7 @@ extern "C" size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* a) {
   if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->batch > INT_MAX / a->heads ||
       a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128))
     return 0;
-  return fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4);
+  return 2 * fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4);  // D, LSE * log2(e)
 }
 
 extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes,
@@ -619,18 +619,20 @@ extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* worksp
       !fav4::encode_bshd(&tdo, a->dout, a->batch, a->sq, a->heads))
     return cudaErrorInvalidValue;
   float* dsum = static_cast<float*>(workspace);
+  float* lse2 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
+                                         fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4));
   {
     const int64_t rows = static_cast<int64_t>(a->batch) * a->sq * a->heads;
     const int64_t want = (rows + 7) / 8;
     const int64_t cap = static_cast<int64_t>(info.sms) * 16;
     fav4::attn_bwd_dsum_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), dsum, a->batch, a->sq,
-        a->heads);
+        static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, dsum, lse2,
+        a->batch, a->sq, a->heads);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   fav4::BwdParams p = {};
-  p.lse = a->lse;
+  p.lse2 = lse2;
   p.dsum = dsum;
   p.batch = a->batch;
   p.heads = a->heads;

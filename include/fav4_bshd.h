@@ -147,8 +147,8 @@ struct Fav4BwdArgs {
 };
 typedef struct Fav4BwdArgs Fav4BwdArgs;
 
-/* Device workspace fav4_bshd_backward needs (D = rowsum(dO * O), FP32
- * [batch, heads, sq]); 0 on invalid arguments. */
+/* Device workspace fav4_bshd_backward needs (D = rowsum(dO * O) and
+ * LSE * log2(e), FP32 [batch, heads, sq] each); 0 on invalid arguments. */
 size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* args);
 
 /* dQ, dK, dV of O = softmax(Q K^T * scale) V (causal: top-left). Three

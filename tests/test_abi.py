@@ -223,7 +223,7 @@ def test_backward_rejects_invalid_arguments(lib):
                          a["heads"], a["sq"], a["sk"], a["scale"])
     good = bwd()
     need = lib.fav4_bshd_backward_workspace_bytes(C.byref(good))
-    assert need == (2 * 4 * 64 * 4 + 255) // 256 * 256
+    assert need == 2 * ((2 * 4 * 64 * 4 + 255) // 256 * 256)
     ws = A16 * 256
     f = lib.fav4_bshd_backward
     for kw in (dict(q=None), dict(dout=None), dict(lse=None), dict(dk=None), dict(batch=0), dict(sk=0),
