@@ -56,19 +56,27 @@ struct FwdParams {
   int num_mblocks;       // query blocks of QTILES*128 rows per (batch, head)
   int num_base_tiles;    // batch * heads * num_mblocks
   int num_tiles;         // num_base_tiles * splits
+  const int* cu_q;        // packed sequences (Varlen): batch + 1 row offsets into Q / O (sq = total rows)
+  const int* cu_k;        //   and into K / V (sk = total keys)
   uint32_t* status;
   uint64_t wait_limit_ns;
 };
 
 struct TileCoord {
-  int b, h, m0;          // m0 = first query row of the work tile
+  int b, h, m0;          // m0 = first query row of the work tile (within its sequence)
   int split;             // KV split of the work tile
-  int kv_begin, kv_end;  // keys it attends
+  int kv_begin, kv_end;  // keys it attends (within its sequence)
+  int sq;                // query rows of its sequence
+  int q0, k0;            // first row of its sequence in Q / O and in K / V (packed sequences)
+  int tb, ob;            // batch coordinate of Q/K/V and of O / LSE (split slices, packed: 0)
 };
 
 // Split: the launch has a key-range index (p.splits > 1); without it every
 // work tile attends [p.kv_begin, p.kv_end) and the index is a constant 0.
-template <bool Causal, int QTiles, bool Split = false>
+// Varlen: batch entry b is the packed sequence [cu_q[b], cu_q[b+1]) of Q / O
+// against [cu_k[b], cu_k[b+1]) of K / V; offsets are clamped to the tensors,
+// so malformed offsets cannot move an access outside them.
+template <bool Causal, int QTiles, bool Split = false, bool Varlen = false>
 __device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
   TileCoord c;
   if (Split) {
@@ -93,13 +101,30 @@ __device__ __forceinline__ TileCoord tile_coord(const FwdParams& p, int t) {
     c.h = bh - c.b * p.heads;
     c.m0 = (t - bh * p.num_mblocks) * (QTiles * kBlockM);
   }
+  if (Varlen) {
+    const int qa = min(max(__ldg(p.cu_q + c.b), 0), p.sq), qe = min(max(__ldg(p.cu_q + c.b + 1), qa), p.sq);
+    const int ka = min(max(__ldg(p.cu_k + c.b), 0), p.sk), ke = min(max(__ldg(p.cu_k + c.b + 1), ka), p.sk);
+    c.q0 = qa;
+    c.sq = qe - qa;
+    c.k0 = ka;
+    c.kv_begin = 0;
+    c.kv_end = ke - ka;
+    c.tb = 0;
+    c.ob = 0;
+  } else {
+    c.q0 = 0;
+    c.k0 = 0;
+    c.sq = p.sq;
+    c.tb = c.b;
+    c.ob = c.split * p.batch + c.b;
+  }
   return c;
 }
 
 // Number of K/V tiles the Q tile at row r0 of work tile `c` needs (0 = tile skipped).
 template <bool Causal>
 __device__ __forceinline__ int kv_tiles_for(const FwdParams& p, const TileCoord& c, int r0) {
-  if (r0 >= p.sq) return 0;  // no real query row in this Q tile
+  if (r0 >= c.sq) return 0;  // no real query row in this Q tile
   int hi = c.kv_end;
   if (Causal) hi = min(hi, r0 + kBlockM);  // top-left causal: key c visible to row r iff c <= r
   if (hi <= c.kv_begin) return 0;
@@ -228,7 +253,7 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 }
 
 // ---------------------------------------------------------------------------
-template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split>
+template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split, bool Varlen>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -297,7 +322,7 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t armed_mask = 0, armed_par = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
+        const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
@@ -310,8 +335,8 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < QTiles; ++i) {
           if ((i == 0 ? n0 : n1) == 0) continue;
           const uint32_t dst = sbase + L::kQ + i * kTileBytes;
-          tma_load_4d(dst, &tm_q, bar(L::kQFull), 0, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
-          tma_load_4d(dst + kBoxBytes, &tm_q, bar(L::kQFull), 64, tc.h, tc.m0 + i * kBlockM, tc.b, pol_q);
+          tma_load_4d(dst, &tm_q, bar(L::kQFull), 0, tc.h, tc.q0 + tc.m0 + i * kBlockM, tc.tb, pol_q);
+          tma_load_4d(dst + kBoxBytes, &tm_q, bar(L::kQFull), 64, tc.h, tc.q0 + tc.m0 + i * kBlockM, tc.tb, pol_q);
         }
         for (int g = -1; g < N && ok; ++g) {
           if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
@@ -325,14 +350,14 @@ __global__ void __launch_bounds__(384, 1)
           armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
           const uint32_t dst = sbase + L::kKV + ring.stage * L::kSlotBytes;
           if (has_v) {
-            const int sv = tc.kv_begin + g * kBlockN;
-            tma_load_4d(dst, &tm_v, fb, 0, kvh, sv, tc.b, pol_kv);
-            tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, kvh, sv, tc.b, pol_kv);
+            const int sv = tc.k0 + tc.kv_begin + g * kBlockN;
+            tma_load_4d(dst, &tm_v, fb, 0, kvh, sv, tc.tb, pol_kv);
+            tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, kvh, sv, tc.tb, pol_kv);
           }
           if (has_k) {
-            const int sk0 = tc.kv_begin + (g + 1) * kBlockN;
-            tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, kvh, sk0, tc.b, pol_kv);
-            tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, kvh, sk0, tc.b, pol_kv);
+            const int sk0 = tc.k0 + tc.kv_begin + (g + 1) * kBlockN;
+            tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, kvh, sk0, tc.tb, pol_kv);
+            tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, kvh, sk0, tc.tb, pol_kv);
           }
           ring.advance<Slots>();
         }
@@ -387,7 +412,7 @@ __global__ void __launch_bounds__(384, 1)
         for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
       };
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
+        const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
         const int N = max(n0, n1);
@@ -463,13 +488,13 @@ __global__ void __launch_bounds__(384, 1)
     const float scale_log2 = p.scale_log2;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      const TileCoord tc = tile_coord<Causal, QTiles, Split>(p, t);
+      const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
       const int r0 = tc.m0 + i * kBlockM;
       const int ni = kv_tiles_for<Causal>(p, tc, r0);
       const int grow = r0 + row;  // query row (global within the sequence)
       float m = -INFINITY, l = 0.f;
       if (ni == 0) {
-        if (r0 >= p.sq) continue;  // padding-only Q tile: nothing to write
+        if (r0 >= tc.sq) continue;  // padding-only Q tile: nothing to write
       }
       for (int j = 0; j < ni; ++j) {
         if (!warp_wait(bar(L::kSFull + i), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
@@ -539,7 +564,9 @@ __global__ void __launch_bounds__(384, 1)
         if (lane == 0) mbar_arrive(bar(L::kPFull + i));
       }
       // ------------------------------ epilogue ------------------------------
-      const bool live = grow < p.sq;
+      const bool live = grow < tc.sq;
+      // O row of this thread: [ob][q0 + grow] in a tensor of sq rows per batch entry
+      const int64_t orow = (static_cast<int64_t>(tc.ob) * p.sq + tc.q0 + grow) * p.heads + tc.h;
       if (ni > 0) {
         // The four warps of this warpgroup meet at 128-thread AND-barriers
         // (id 1 + i); a warp that gave up on a wait above arrives with
@@ -550,6 +577,9 @@ __global__ void __launch_bounds__(384, 1)
         o_full_par ^= 1u;
         tc_fence_after();
         const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+        // The ragged last Q tile of a packed sequence is stored row by row: a 128-row TMA box would
+        // also write the next sequence's rows. Tile-uniform, so all four warps take the same path.
+        const bool direct = Varlen && r0 + kBlockM > tc.sq;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t pk[32];
@@ -566,7 +596,15 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_before();
             __syncwarp();  // every lane has read its row of O_i
             if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
-            pair_all(1 + i, 128, true);  // the store of columns 0-63 has read the stage
+            if (!direct) pair_all(1 + i, 128, true);  // the store of columns 0-63 has read the stage
+          }
+          if (direct) {
+            if (live) {
+              uint4* dst = reinterpret_cast<uint4*>(p.o + orow * kHeadDim + half * 64);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) dst[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            }
+            continue;
           }
 #pragma unroll
           for (int c = 0; c < 8; ++c)
@@ -575,21 +613,20 @@ __global__ void __launch_bounds__(384, 1)
           fence_proxy_async_smem();
           pair_all(1 + i, 128, true);  // every row of this half is staged
           if (issuer) {
-            tma_store_4d(&tm_o, stage, half * 64, tc.h, r0, tc.split * p.batch + tc.b);  // O map: splits x batch
+            tma_store_4d(&tm_o, stage, half * 64, tc.h, tc.q0 + r0, tc.ob);  // O map: batch = splits x batch
             tma_store_commit();
             if (half == 0) tma_store_wait_read_all();
           }
         }
       } else if (live) {
-        // no key visible to this Q tile (a split-KV slice): O = 0
-        const int64_t bs = static_cast<int64_t>(tc.split) * p.batch + tc.b;  // batch row in the split slices
-        uint4* dst = reinterpret_cast<uint4*>(p.o + ((bs * p.sq + grow) * p.heads + tc.h) * kHeadDim);
+        // no key visible to this Q tile (a split-KV slice, an empty key sequence): O = 0
+        uint4* dst = reinterpret_cast<uint4*>(p.o + orow * kHeadDim);
 #pragma unroll
         for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0u, 0u, 0u, 0u);
       }
       if (!ok) break;
       if (live && p.lse != nullptr) {
-        p.lse[((static_cast<int64_t>(tc.split) * p.batch + tc.b) * p.heads + tc.h) * p.sq + grow] =
+        p.lse[(static_cast<int64_t>(tc.ob) * p.heads + tc.h) * p.sq + tc.q0 + grow] =
             l > 0.f ? m * kLn2 + logf(l) : -INFINITY;
       }
     }

@@ -84,14 +84,18 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
 //   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
 //   3: as 2 with 1/2 of exp2 on the polynomial
-template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split>
-int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int splits, cudaStream_t stream) {
+// Varlen: a.sq / a.sk are the packed row counts, a.batch the number of
+// sequences, cu_q / cu_k their device offsets and max_sq the longest query
+// sequence (it sizes the tile grid).
+template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split, bool Varlen = false>
+int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int splits, cudaStream_t stream,
+               const int* cu_q = nullptr, const int* cu_k = nullptr, int max_sq = 0) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   DeviceInfo info;
   if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
-  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split>;
+  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split, Varlen>;
   constexpr int smem = SmemLayout<QTiles, Slots>::kAlloc;
   {
     static std::mutex mu;
@@ -104,8 +108,9 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int sp
     }
   }
   CUtensorMap tq, tk, tv, to;
-  if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, kv_heads) ||
-      !encode_bshd(&tv, a.v, a.batch, a.sk, kv_heads) || !encode_bshd(&to, a.o, a.batch * splits, a.sq, a.heads))
+  const int mb = Varlen ? 1 : a.batch;  // packed sequences: one batch entry of sq / sk rows
+  if (!encode_bshd(&tq, a.q, mb, a.sq, a.heads) || !encode_bshd(&tk, a.k, mb, a.sk, kv_heads) ||
+      !encode_bshd(&tv, a.v, mb, a.sk, kv_heads) || !encode_bshd(&to, a.o, mb * splits, a.sq, a.heads))
     return cudaErrorInvalidValue;
   FwdParams p;
   p.o = static_cast<__nv_bfloat16*>(a.o);
@@ -121,7 +126,9 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int sp
   // whole 128-key tiles per split
   p.kv_chunk = ((kv_end - kv_begin + splits - 1) / splits + kBlockN - 1) / kBlockN * kBlockN;
   p.scale_log2 = a.scale * 1.4426950408889634f;
-  p.num_mblocks = (a.sq + QTiles * kBlockM - 1) / (QTiles * kBlockM);
+  p.num_mblocks = ((Varlen ? max_sq : a.sq) + QTiles * kBlockM - 1) / (QTiles * kBlockM);
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
   const int64_t base = static_cast<int64_t>(a.batch) * a.heads * p.num_mblocks;
   const int64_t tiles = base * splits;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
@@ -140,16 +147,16 @@ int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream
   if (kv_heads == 0) kv_heads = a.heads;
   if (splits > 1) {  // the work tiles carry a key-range index
     switch (config) {
-      case 1: return launch_fwd<Causal, 1, 2, 0, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
-      case 2: return launch_fwd<Causal, 2, 2, 2, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
-      case 3: return launch_fwd<Causal, 2, 2, 4, true>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 1: return launch_fwd<Causal, 1, 2, 0, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 2: return launch_fwd<Causal, 2, 2, 2, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 3: return launch_fwd<Causal, 2, 2, 4, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (config) {
-    case 1: return launch_fwd<Causal, 1, 2, 0, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
-    case 2: return launch_fwd<Causal, 2, 2, 2, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
-    case 3: return launch_fwd<Causal, 2, 2, 4, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 1: return launch_fwd<Causal, 1, 2, 0, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 2: return launch_fwd<Causal, 2, 2, 2, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 4, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -158,6 +165,48 @@ int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream
 }  // namespace fav4
 
 extern "C" int fav4_bshd_select_config(const Fav4Args* a) { return a->sq < 128 ? 1 : 2; }
+
+namespace fav4 {
+namespace {
+
+template <bool Causal>
+int dispatch_varlen(const Fav4Args& a, int config, int kv_heads, const int* cu_q, const int* cu_k, int max_sq,
+                    cudaStream_t stream) {
+  switch (config) {
+    case 1: return launch_fwd<Causal, 1, 2, 0, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
+    case 2: return launch_fwd<Causal, 2, 2, 2, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
+    case 3: return launch_fwd<Causal, 2, 2, 4, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_forward_varlen(const Fav4VarlenArgs* v, int causal, int config, cudaStream_t stream) {
+  if (!v || !v->cu_seqlens_q || !v->cu_seqlens_k || v->max_sq <= 0 || v->max_sq > v->total_q || v->kv_heads < 1 ||
+      v->heads < 1 || v->kv_heads > v->heads || v->heads % v->kv_heads ||
+      (reinterpret_cast<uintptr_t>(v->cu_seqlens_q) & 3) || (reinterpret_cast<uintptr_t>(v->cu_seqlens_k) & 3))
+    return cudaErrorInvalidValue;
+  Fav4Args a;
+  a.q = v->q;
+  a.k = v->k;
+  a.v = v->v;
+  a.o = v->o;
+  a.lse = v->lse;
+  a.batch = v->batch;
+  a.heads = v->heads;
+  a.sq = v->total_q;
+  a.sk = v->total_k;
+  a.scale = v->scale;
+  if (!fav4::args_valid(&a, causal, config) || (v->lse && (reinterpret_cast<uintptr_t>(v->lse) & 3)))
+    return cudaErrorInvalidValue;
+  if (config == 0) config = v->max_sq < 128 ? 1 : 2;
+  return causal ? fav4::dispatch_varlen<true>(a, config, v->kv_heads, v->cu_seqlens_q, v->cu_seqlens_k, v->max_sq,
+                                              stream)
+                : fav4::dispatch_varlen<false>(a, config, v->kv_heads, v->cu_seqlens_q, v->cu_seqlens_k, v->max_sq,
+                                               stream);
+}
 
 extern "C" int fav4_bshd_forward(const Fav4Args* a, int causal, int config, cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config)) return cudaErrorInvalidValue;

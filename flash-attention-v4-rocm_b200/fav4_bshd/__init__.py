@@ -35,6 +35,13 @@ class BwdArgs(C.Structure):
         (n, C.c_int) for n in ("batch", "heads", "sq", "sk")] + [("scale", C.c_float)]
 
 
+class VarlenArgs(C.Structure):
+    """Fav4VarlenArgs (include/fav4_bshd.h): packed variable-length sequences."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "lse", "cu_seqlens_q", "cu_seqlens_k")] + [
+        (n, C.c_int) for n in ("batch", "heads", "kv_heads", "max_sq", "total_q", "total_k")] + [("scale", C.c_float)]
+
+
 class HostOut(C.Structure):
     """Fav4HostOut (include/fav4_bshd.h): one output of fav4_bshd_forward_host."""
 
@@ -78,6 +85,8 @@ def _bind(lib):
     lib.fav4_bshd_backward_workspace_bytes.restype = C.c_size_t
     lib.fav4_bshd_backward.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.fav4_bshd_backward.restype = C.c_int
+    lib.fav4_bshd_forward_varlen.argtypes = [C.POINTER(VarlenArgs), C.c_int, C.c_int, C.c_void_p]
+    lib.fav4_bshd_forward_varlen.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
     lib.fav4_bshd_pipeline_status.restype = C.c_int
     return lib
@@ -266,6 +275,25 @@ class Runner:
         if status:
             raise RuntimeError(f"forward_host: CUDA status {status}")
 
+    def call_varlen(self, q, k, v, o, lse, cu_q, cu_k, max_sq, causal, config=0, scale=None, stream=None):
+        """Packed sequences (fav4_bshd_forward_varlen): q, o [total_q, H, 128];
+        k, v [total_k, H_kv, 128]; cu_q, cu_k int32 CUDA [batch + 1]; lse
+        optional FP32 [H, total_q]."""
+        import torch
+        for x in (q, k, v, o):
+            assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous() and x.dim() == 3
+        assert cu_q.dtype == cu_k.dtype == torch.int32 and cu_q.is_cuda and cu_k.is_cuda
+        assert cu_q.numel() == cu_k.numel() >= 2 and o.shape == q.shape and k.shape == v.shape
+        tq, h, _ = q.shape
+        tk, hk, _ = k.shape
+        assert lse is None or (lse.shape == (h, tq) and lse.dtype == torch.float32 and lse.is_contiguous())
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        a = VarlenArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _ptr(lse), cu_q.data_ptr(),
+                       cu_k.data_ptr(), cu_q.numel() - 1, h, hk, max_sq, tq, tk, scale)
+        status = self.lib.fav4_bshd_forward_varlen(C.byref(a), int(causal), config, _stream(stream))
+        if status:
+            raise RuntimeError(f"varlen config {config}: CUDA status {status}")
+
     def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None):
         """dQ, dK, dV through fav4_bshd_backward (all BF16 BSHD CUDA tensors,
         lse the forward's FP32 [B, H, Sq]). The D workspace is allocated with
@@ -305,5 +333,5 @@ def forward(q, k, v, causal=False, config=0, scale=None, return_lse=False, out=N
     return (o, lse) if return_lse else o
 
 
-__all__ = ["Args", "BwdArgs", "HostOut", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
+__all__ = ["Args", "BwdArgs", "VarlenArgs", "HostOut", "Runner", "forward", "load_library", "load_probe_library", "LIB_PATH", "PROBE_LIB_PATH",
            "HEAD_DIM", "CUDA_ERROR_INVALID_VALUE"]

@@ -19,8 +19,10 @@ output allocation, the current stream and tracing:
 The CUDA kernel runs through ``fav4_bshd_forward`` on the current stream, so
 the operator can be captured in a CUDA graph. A fake (meta) implementation
 gives shapes to FakeTensor tracing and ``torch.compile`` graphs, so the op
-composes with both. It has no autograd formula: the library implements the
-forward pass only, and asking for a gradient raises.
+composes with both. Gradients of O with respect to q, k, v come from
+``fav4_bshd_backward``; they need the LSE, so call the op with
+``return_lse=True`` (``attention()`` does). A gradient through the LSE output
+and grouped-query gradients are not implemented and raise.
 """
 from __future__ import annotations
 
@@ -76,8 +78,38 @@ def _(q, k, v, causal, config, scale, return_lse):
     return o, lse
 
 
+def _setup_context(ctx, inputs, output):
+    q, k, v, causal, config, scale, return_lse = inputs
+    o, lse = output
+    ctx.save_for_backward(q, k, v, o, lse)
+    ctx.causal, ctx.has_lse = causal, return_lse
+    ctx.scale = 1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale
+    ctx.set_materialize_grads(False)
+
+
+def _backward(ctx, grad_o, grad_lse):
+    q, k, v, o, lse = ctx.saved_tensors
+    if grad_lse is not None:
+        raise NotImplementedError("fav4::bshd_forward: the gradient through the LSE output is not implemented")
+    if not ctx.has_lse:
+        raise RuntimeError("fav4::bshd_forward: gradients need return_lse=True (fav4_bshd.ops.attention does this)")
+    if k.shape[2] != q.shape[2]:
+        raise NotImplementedError("fav4::bshd_forward: grouped-query gradients are not implemented")
+    if grad_o is None:
+        return None, None, None, None, None, None, None
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    with torch.cuda.device(q.device):
+        _runner().backward(q.contiguous(), k.contiguous(), v.contiguous(), o, grad_o.contiguous(), lse, dq, dk, dv,
+                           ctx.causal, ctx.scale)
+    return dq, dk, dv, None, None, None, None
+
+
+bshd_forward.register_autograd(_backward, setup_context=_setup_context)
+
+
 def attention(q, k, v, causal: bool = False, config: int = 0, scale: float | None = None,
               return_lse: bool = False):
-    """Convenience wrapper: O, or (O, LSE) when ``return_lse``."""
-    o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, -1.0 if scale is None else scale, return_lse)
+    """O, or (O, LSE) when ``return_lse``; differentiable in q, k, v (the LSE
+    is always computed so that the backward pass can use it)."""
+    o, lse = torch.ops.fav4.bshd_forward(q, k, v, causal, config, -1.0 if scale is None else scale, True)
     return (o, lse) if return_lse else o

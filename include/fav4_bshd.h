@@ -55,6 +55,30 @@ int fav4_bshd_select_config(const Fav4Args* args);
  * cudaErrorInvalidValue when kv_heads is not a divisor of heads. */
 int fav4_bshd_forward_gqa(const Fav4Args* args, int kv_heads, int causal, int config, cudaStream_t stream);
 
+/* Packed variable-length sequences (no reference counterpart). Sequence b has
+ * query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of q / o and keys
+ * [cu_seqlens_k[b], cu_seqlens_k[b+1]) of k / v; the offset arrays are device
+ * int32 [batch + 1]. q, o: BF16 [total_q, heads, 128]; k, v: BF16
+ * [total_k, kv_heads, 128] (kv_heads divides heads; equal heads for ordinary
+ * attention); lse (optional): FP32 [heads, total_q]. max_sq: the longest query
+ * sequence (at most total_q; it sizes the launch). Causal masking is
+ * top-left within each sequence, as in fav4_bshd_forward. Offsets are read on
+ * the device and clamped to [0, total]: malformed offsets give wrong rows,
+ * never an access outside the tensors. Returns 0, cudaErrorInvalidValue or the
+ * launch status. */
+struct Fav4VarlenArgs {
+  const void *q, *k, *v;
+  void* o;
+  float* lse;
+  const int* cu_seqlens_q;
+  const int* cu_seqlens_k;
+  int batch, heads, kv_heads, max_sq, total_q, total_k;
+  float scale;
+};
+typedef struct Fav4VarlenArgs Fav4VarlenArgs;
+
+int fav4_bshd_forward_varlen(const Fav4VarlenArgs* args, int causal, int config, cudaStream_t stream);
+
 /* Split-KV slice (no reference counterpart; needed because Fav4Args carries
  * no key offset). Attends only keys [kv_begin, kv_end) with absolute
  * positions, so top-left causal masking stays correct for any slice. O is the

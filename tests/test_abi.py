@@ -234,3 +234,20 @@ def test_backward_rejects_invalid_arguments(lib):
     assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
     assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
     assert f(C.byref(good), 0, None, need, None) == INVALID
+
+
+def test_varlen_rejects_invalid_arguments(lib):
+    def va(**kw):
+        a = dict(q=A16, k=A16 * 2, v=A16 * 3, o=A16 * 4, lse=None, cu_seqlens_q=A16 * 5, cu_seqlens_k=A16 * 6,
+                 batch=3, heads=8, kv_heads=8, max_sq=100, total_q=200, total_k=300, scale=0.1)
+        a.update(kw)
+        return F.VarlenArgs(*(a[n] for n in ("q", "k", "v", "o", "lse", "cu_seqlens_q", "cu_seqlens_k", "batch",
+                                             "heads", "kv_heads", "max_sq", "total_q", "total_k", "scale")))
+    f = lib.fav4_bshd_forward_varlen
+    for kw in (dict(q=None), dict(o=None), dict(cu_seqlens_q=None), dict(cu_seqlens_k=None), dict(batch=0),
+               dict(max_sq=0), dict(max_sq=201), dict(kv_heads=3), dict(kv_heads=0), dict(total_k=0),
+               dict(scale=-1.0), dict(cu_seqlens_q=A16 * 5 + 2), dict(lse=A16 * 7 + 1), dict(k=A16 + 8)):
+        assert f(C.byref(va(**kw)), 0, 0, None) == INVALID, kw
+    assert f(C.byref(va()), 2, 0, None) == INVALID
+    assert f(C.byref(va()), 0, 5, None) == INVALID
+    assert f(None, 0, 0, None) == INVALID

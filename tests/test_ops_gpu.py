@@ -68,9 +68,31 @@ def test_cuda_graph_capture_replays():
     assert torch.equal(out, want)
 
 
-def test_gradient_is_not_silent():
-    q, k, v = _inputs(1, 2, 128, 128, seed=8)
-    q.requires_grad_(True)
+def test_gradients_through_the_operator(runner):
+    q, k, v = _inputs(2, 4, 300, 300, seed=8)
+    do = torch.randn_like(q)
+    qg, kg, vg = (x.clone().requires_grad_(True) for x in (q, k, v))
+    o = ops.attention(qg, kg, vg, causal=True)
+    o.backward(do)
+    # the same C ABI calls by hand
+    lse = torch.empty((2, 4, 300), device="cuda")
+    o2 = torch.empty_like(q)
+    runner.call(q, k, v, o2, lse, True, 0, 1 / math.sqrt(128))
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    runner.backward(q, k, v, o2, do, lse, dq, dk, dv, True, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert torch.equal(o.detach(), o2)
+    assert torch.equal(qg.grad, dq) and torch.equal(kg.grad, dk) and torch.equal(vg.grad, vg.grad)
+    assert torch.equal(vg.grad, dv)
+
+
+def test_gradient_limits_raise():
+    q, k, v = _inputs(1, 2, 128, 128, seed=10)
+    qg = q.clone().requires_grad_(True)
+    o, lse = torch.ops.fav4.bshd_forward(qg, k, v, False, 0, -1.0, False)  # no LSE kept
     with pytest.raises(RuntimeError):
-        o = ops.attention(q, k, v)
         o.float().sum().backward()
+    qg = q.clone().requires_grad_(True)
+    o, lse = ops.attention(qg, k, v, return_lse=True)
+    with pytest.raises(NotImplementedError):
+        (o.float().sum() + lse.sum()).backward()

@@ -1,0 +1,73 @@
+"""GPU tests of packed variable-length sequences (fav4_bshd_forward_varlen):
+every sequence's output and LSE are bit-identical to fav4_bshd_forward on
+that sequence alone (ragged lengths, empty sequences, Sq != Sk, GQA, dense
+and top-left causal, every config), and malformed offsets stay inside the
+tensors (clamped on the device)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _packed(lens_q, lens_k, h, hk, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    tq, tk = sum(lens_q), sum(lens_k)
+    q = torch.randn((max(tq, 1), h, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn((max(tk, 1), hk, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn((max(tk, 1), hk, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    cu = lambda lens: torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device="cuda", dtype=torch.int32)  # noqa
+    return q, k, v, cu(lens_q), cu(lens_k)
+
+
+CASES = [((1, 129, 1000, 300), (5, 200, 1537, 128), 4, 4), ((256, 0, 77, 640), (256, 300, 77, 0), 2, 2),
+         ((513, 2048), (513, 2048), 8, 2), ((64,) * 7, (4000, 1, 2, 3, 4, 5, 6), 2, 1)]
+
+
+@pytest.mark.parametrize("lens_q,lens_k,h,hk", CASES)
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("config", [0, 1, 3])
+def test_varlen_equals_per_sequence_forward(runner, lens_q, lens_k, h, hk, causal, config):
+    q, k, v, cu_q, cu_k = _packed(lens_q, lens_k, h, hk, seed=len(lens_q) * 10 + h)
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((h, q.shape[0]), float("nan"), device="cuda")
+    runner.call_varlen(q, k, v, o, lse, cu_q, cu_k, max(lens_q), causal, config)
+    torch.cuda.synchronize()
+    for b, (nq, nk) in enumerate(zip(lens_q, lens_k)):
+        if nq == 0:
+            continue
+        q0, k0 = int(cu_q[b]), int(cu_k[b])
+        got_o, got_l = o[q0:q0 + nq], lse[:, q0:q0 + nq]
+        if nk == 0:
+            assert torch.count_nonzero(got_o) == 0 and torch.isneginf(got_l).all()
+            continue
+        qs = q[q0:q0 + nq].unsqueeze(0).contiguous()
+        ks, vs = (x[k0:k0 + nk].unsqueeze(0).contiguous() for x in (k, v))
+        want_o = torch.empty_like(qs)
+        want_l = torch.empty((1, h, nq), device="cuda")
+        cfg = config if config else (1 if max(lens_q) < 128 else 2)
+        if hk == h:
+            runner.call(qs, ks, vs, want_o, want_l, causal, cfg)
+        else:
+            runner.call_gqa(qs, ks, vs, want_o, want_l, causal, cfg)
+        torch.cuda.synchronize()
+        assert torch.equal(got_o, want_o[0]), (b, nq, nk)
+        assert torch.equal(got_l, want_l[0]), (b, nq, nk)
+    assert runner.pipeline_status() == 0
+
+
+def test_varlen_malformed_offsets_stay_inside(runner):
+    # offsets beyond the totals and decreasing offsets are clamped on the device
+    h = 2
+    q = torch.randn((300, h, 128), device="cuda", dtype=torch.bfloat16)
+    k = torch.randn((200, h, 128), device="cuda", dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    canary = torch.full((300 + 64, h, 128), 7.0, device="cuda", dtype=torch.bfloat16)
+    o = canary[:300]
+    cu_q = torch.tensor([0, 250, 100, 10_000], device="cuda", dtype=torch.int32)
+    cu_k = torch.tensor([0, 999, 50, 200], device="cuda", dtype=torch.int32)
+    runner.call_varlen(q, k, v, o, None, cu_q, cu_k, 300, False, 0)
+    torch.cuda.synchronize()
+    assert torch.all(canary[300:] == 7.0)
+    assert runner.pipeline_status() == 0
