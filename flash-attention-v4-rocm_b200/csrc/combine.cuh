@@ -11,11 +11,12 @@
 
 namespace fav4 {
 
-constexpr int kMaxCombineParts = 16;
+constexpr int kMaxCombineParts = 16;   // parts accepted by the public combine entry point
+constexpr int kCombineCapacity = 32;   // parts the kernel handles (the one-launch split-KV uses up to 32)
 
 struct CombineParams {
-  const __nv_bfloat16* o[kMaxCombineParts];
-  const float* lse[kMaxCombineParts];
+  const __nv_bfloat16* o[kCombineCapacity];
+  const float* lse[kCombineCapacity];
   int parts;
   __nv_bfloat16* out;
   float* lse_out;
@@ -34,9 +35,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ Co
     const int b = static_cast<int>(br / p.sq);
     const int64_t lse_idx = (static_cast<int64_t>(b) * p.heads + h) * p.sq + r;
     float mx = -INFINITY;
-    float lg[kMaxCombineParts];
+    float lg[kCombineCapacity];
 #pragma unroll
-    for (int g = 0; g < kMaxCombineParts; ++g) {
+    for (int g = 0; g < kCombineCapacity; ++g) {
       if (g < p.parts) {
         lg[g] = p.lse[g][lse_idx];
         mx = fmaxf(mx, lg[g]);
@@ -46,7 +47,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ Co
     float wsum = 0.f;
     if (mx != -INFINITY) {
 #pragma unroll
-      for (int g = 0; g < kMaxCombineParts; ++g) {
+      for (int g = 0; g < kCombineCapacity; ++g) {
         if (g < p.parts && lg[g] != -INFINITY) {
           const float w = expf(lg[g] - mx);
           wsum += w;

@@ -234,13 +234,17 @@ extern "C" int fav4_bshd_forward_partial(const Fav4Args* a, int causal, int conf
                 : fav4::dispatch<false>(*a, config, kv_begin, kv_end, stream);
 }
 
-extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts, int parts, void* o,
-                                 float* lse, int batch, int heads, int sq, cudaStream_t stream) {
-  if (!o_parts || !lse_parts || !o || parts < 1 || parts > fav4::kMaxCombineParts || batch <= 0 || heads <= 0 ||
+namespace fav4 {
+namespace {
+
+// The combine launch for 1..kCombineCapacity parts (arguments validated as fav4_bshd_combine does).
+int combine_parts(const void* const* o_parts, const float* const* lse_parts, int parts, void* o, float* lse,
+                  int batch, int heads, int sq, cudaStream_t stream) {
+  if (!o_parts || !lse_parts || !o || parts < 1 || parts > kCombineCapacity || batch <= 0 || heads <= 0 ||
       sq <= 0 || batch > INT_MAX / heads || heads > INT_MAX / 128 || sq > INT_MAX / (heads * 128) ||
       (reinterpret_cast<uintptr_t>(o) & 15))
     return cudaErrorInvalidValue;
-  fav4::CombineParams p = {};
+  CombineParams p = {};
   for (int g = 0; g < parts; ++g) {
     if (!o_parts[g] || !lse_parts[g] || (reinterpret_cast<uintptr_t>(o_parts[g]) & 15) ||
         (reinterpret_cast<uintptr_t>(lse_parts[g]) & 3))
@@ -257,14 +261,23 @@ extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const*
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  fav4::DeviceInfo info;
-  if (!fav4::device_info(dev, &info)) return cudaErrorInvalidDevice;
+  DeviceInfo info;
+  if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
   const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
   const int64_t want = (rows + 7) / 8;  // 8 warps per block, one row per warp per pass
   const int64_t cap = static_cast<int64_t>(info.sms) * 8;
   const int grid = static_cast<int>(want < cap ? want : cap);
-  fav4::combine_kernel<<<grid, 256, 0, stream>>>(p);
+  combine_kernel<<<grid, 256, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts, int parts, void* o,
+                                 float* lse, int batch, int heads, int sq, cudaStream_t stream) {
+  if (parts > fav4::kMaxCombineParts) return cudaErrorInvalidValue;
+  return fav4::combine_parts(o_parts, lse_parts, parts, o, lse, batch, heads, sq, stream);
 }
 
 // --------------------------------------------------------------------------
@@ -523,15 +536,15 @@ extern "C" int fav4_bshd_splitkv_splits(const Fav4Args* a, int causal, int confi
   // keys any query row can see (top-left causal: rows < sq see keys < sq)
   const int keys = causal ? (a->sq < a->sk ? a->sq : a->sk) : a->sk;
   const int64_t kv_tiles = (keys + fav4::kBlockN - 1) / fav4::kBlockN;
-  // enough work tiles to fill the SMs, at least 4 K/V tiles (512 keys) per split, at most 16 splits
-  int64_t splits = (info.sms + base - 1) / base;
+  // as many work tiles as fit one wave over the SMs, at least 4 K/V tiles (512 keys) per split, at most 32
+  int64_t splits = info.sms / base;
   if (splits > kv_tiles / 4) splits = kv_tiles / 4;
-  if (splits > fav4::kMaxCombineParts) splits = fav4::kMaxCombineParts;
+  if (splits > fav4::kCombineCapacity) splits = fav4::kCombineCapacity;
   return splits < 1 ? 1 : static_cast<int>(splits);
 }
 
 extern "C" size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* a, int splits) {
-  if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || splits < 1 || splits > fav4::kMaxCombineParts ||
+  if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || splits < 1 || splits > fav4::kCombineCapacity ||
       a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128))
     return 0;
   if (splits == 1) return 0;
@@ -558,8 +571,8 @@ int splitkv_range(const Fav4Args* a, int causal, int config, int kv_begin, int k
   // o_slice bytes, a multiple of 256), LSE slice s starts s * B*H*Sq values into the LSE region.
   const size_t o_elems = static_cast<size_t>(a->batch) * a->sq * a->heads * kHeadDim;
   const size_t lse_elems = static_cast<size_t>(a->batch) * a->heads * a->sq;
-  const void* o_parts[kMaxCombineParts];
-  const float* lse_parts[kMaxCombineParts];
+  const void* o_parts[kCombineCapacity];
+  const float* lse_parts[kCombineCapacity];
   for (int s = 0; s < splits; ++s) {
     o_parts[s] = ws + s * o_elems * 2;
     lse_parts[s] = reinterpret_cast<const float*>(ws + splits * l.o_slice) + s * lse_elems;
@@ -567,7 +580,7 @@ int splitkv_range(const Fav4Args* a, int causal, int config, int kv_begin, int k
   const int e = causal ? dispatch<true>(pa, config, kv_begin, kv_end, stream, 0, splits)
                        : dispatch<false>(pa, config, kv_begin, kv_end, stream, 0, splits);
   if (e != cudaSuccess) return e;
-  return fav4_bshd_combine(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
+  return combine_parts(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
 }
 
 }  // namespace
@@ -575,7 +588,7 @@ int splitkv_range(const Fav4Args* a, int causal, int config, int kv_begin, int k
 
 extern "C" int fav4_bshd_forward_splitkv(const Fav4Args* a, int causal, int config, int splits, void* workspace,
                                          size_t workspace_bytes, cudaStream_t stream) {
-  if (!fav4::args_valid(a, causal, config) || splits < 0 || splits > fav4::kMaxCombineParts)
+  if (!fav4::args_valid(a, causal, config) || splits < 0 || splits > fav4::kCombineCapacity)
     return cudaErrorInvalidValue;
   if (config == 0) config = fav4_bshd_select_config(a);
   if (splits == 0) splits = fav4_bshd_splitkv_splits(a, causal, config);
@@ -588,7 +601,7 @@ extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, 
                                                  int kv_end, int splits, void* workspace, size_t workspace_bytes,
                                                  cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || !a->lse || kv_begin < 0 || kv_end <= kv_begin || kv_end > a->sk ||
-      (reinterpret_cast<uintptr_t>(a->lse) & 3) || splits < 1 || splits > fav4::kMaxCombineParts)
+      (reinterpret_cast<uintptr_t>(a->lse) & 3) || splits < 1 || splits > fav4::kCombineCapacity)
     return cudaErrorInvalidValue;
   if (config == 0) config = fav4_bshd_select_config(a);
   if (splits == 1) return fav4_bshd_forward_partial(a, causal, config, kv_begin, kv_end, stream);

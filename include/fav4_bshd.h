@@ -129,7 +129,7 @@ int fav4_bshd_forward_splitkv_static(const Fav4Args* args, int causal, int confi
  * `workspace`, and the LSE-weighted combine kernel (fav4_bshd_combine) merges
  * them into args->o / args->lse. Results equal fav4_bshd_forward within the
  * split-KV tolerance (|dO| <= 2e-2, |dLSE| <= 1e-3).
- *   - splits: 1..16, or 0 for fav4_bshd_splitkv_splits(args, causal, config);
+ *   - splits: 1..32, or 0 for fav4_bshd_splitkv_splits(args, causal, config);
  *     1 is fav4_bshd_forward and needs no workspace.
  *   - workspace: device memory, 256-byte aligned, at least
  *     fav4_bshd_splitkv_workspace_bytes(args, splits) bytes; calls sharing a
@@ -139,7 +139,7 @@ int fav4_bshd_forward_splitkv(const Fav4Args* args, int causal, int config, int 
                               size_t workspace_bytes, cudaStream_t stream);
 
 /* fav4_bshd_forward_partial with the one-launch split: keys [kv_begin, kv_end)
- * (absolute positions) in `splits` (1..16) ranges, combined into the slice's
+ * (absolute positions) in `splits` (1..32) ranges, combined into the slice's
  * partial O and its LSE (required), as fav4_bshd_forward_partial returns them.
  * For a GPU that holds one key chunk of a multi-GPU decode step. Validation
  * and return codes as fav4_bshd_forward_partial, workspace as
@@ -152,7 +152,7 @@ int fav4_bshd_forward_partial_splitkv(const Fav4Args* args, int causal, int conf
 size_t fav4_bshd_splitkv_workspace_bytes(const Fav4Args* args, int splits);
 
 /* The automatic number of splits on the current device: enough work tiles to
- * cover its SMs, at least 4 key tiles (512 keys) per split, at most 16. Returns
+ * fit one wave over its SMs, at least 4 key tiles (512 keys) per split, at most 32. Returns
  * 1 when the query tiles alone fill the GPU, -1 on invalid arguments or a CUDA
  * error. */
 int fav4_bshd_splitkv_splits(const Fav4Args* args, int causal, int config);

@@ -196,7 +196,7 @@ def test_splitkv_workspace_bytes(lib):
     assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 5) == 5 * per
     assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 1) == 0
     assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 0) == 0
-    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 17) == 0
+    assert lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 33) == 0
 
 
 def test_splitkv_rejects_invalid_arguments(lib):
@@ -204,7 +204,7 @@ def test_splitkv_rejects_invalid_arguments(lib):
     need = lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 4)
     f = lib.fav4_bshd_forward_splitkv
     ws = A16 * 256
-    assert f(C.byref(a), 0, 0, 17, ws, need, None) == INVALID
+    assert f(C.byref(a), 0, 0, 33, ws, need, None) == INVALID
     assert f(C.byref(a), 0, 0, -1, ws, need, None) == INVALID
     assert f(C.byref(a), 0, 0, 4, ws, need - 1, None) == INVALID      # workspace too small
     assert f(C.byref(a), 0, 0, 4, ws + 128, need, None) == INVALID    # misaligned

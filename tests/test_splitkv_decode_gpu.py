@@ -46,7 +46,7 @@ SHAPES = [(1, 8, 1, 32768), (1, 8, 16, 20000), (2, 4, 64, 8192), (1, 8, 128, 655
 
 @pytest.mark.parametrize("b,h,sq,sk", SHAPES)
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("splits", [0, 2, 7, 16])
+@pytest.mark.parametrize("splits", [0, 2, 7, 16, 32])
 def test_splitkv_matches_forward(runner, b, h, sq, sk, causal, splits):
     q, k, v = _inputs(b, h, sq, sk, seed=sq + sk)
     o_ref, l_ref = _plain(runner, q, k, v, causal, 0)
@@ -104,7 +104,7 @@ def test_automatic_split_count(runner):
         a = F.Args(16, 32, 48, 64, None, b, h, sq, sk, 1 / math.sqrt(128))
         return lib.fav4_bshd_splitkv_splits(C.byref(a), causal, config)
 
-    assert splits(1, 8, 1, 131072) == min(16, -(-sms // 8))
+    assert splits(1, 8, 1, 131072) == min(32, sms // 8)
     assert splits(32, 8, 4096, 4096) == 1
     assert splits(1, 8, 1, 1024) == 2          # at least 4 key tiles per split
     assert splits(1, 8, 1, 131072, causal=1) == 1  # top-left causal: one visible key tile
