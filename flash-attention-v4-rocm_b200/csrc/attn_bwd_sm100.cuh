@@ -54,8 +54,9 @@ struct BwdSmem {
   static constexpr int kInner = 2 * kTileBytes;      // 2 stages x 2 x 32 KiB
   static constexpr int kBar = kInner + 4 * kTileBytes;
   static constexpr int kOuterFull = 0, kOuterEmpty = 1, kInFull = 2, kInEmpty = 4;
-  static constexpr int kSFull = 6, kPFull = 7, kAccFull = 8, kAccEmpty = 9, kTeardown = 10;
-  static constexpr int kNumBars = 11;
+  static constexpr int kSFull = 6, kPFull = 7;  // kPFull: [4] one per 32-column chunk of P^T / dS^T
+  static constexpr int kAccFull = 11, kAccEmpty = 12, kTeardown = 13;
+  static constexpr int kNumBars = 14;
   static constexpr int kTmemHolder = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemHolder + 4;
   static constexpr int kBytes = kAbort + 4;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(bar(L::kInEmpty + s), 1);
     }
     mbar_init(bar(L::kSFull), 1);
-    mbar_init(bar(L::kPFull), 4);     // elementwise warps
+    for (int c = 0; c < 4; ++c) mbar_init(bar(L::kPFull + c), 4);  // elementwise warps, per chunk
     mbar_init(bar(L::kAccFull), 1);
     mbar_init(bar(L::kAccEmpty), 4);  // elementwise warps, after the epilogue read
     mbar_init(bar(L::kTeardown), 1);
@@ -209,12 +210,15 @@ __global__ void __launch_bounds__(192, 1)
           umma_ss_w(tmem + d, aa + off, k_hi, ba + off, k_hi, idesc_ss, k > 0 ? 1u : 0u);
         }
       };
-      // D (tmem column d) (+)= A (tmem column a, BF16 pairs) * B (shared tile b, MN-major)
-      auto mma_ts = [&](uint32_t d, uint32_t a, int b_off, bool acc) {
+      // D (tmem column d) (+)= A (tmem column a, BF16 pairs) * B (shared tile b, MN-major), K steps
+      // [2 ch, 2 ch + 2): the 32 columns of chunk ch
+      auto mma_ts = [&](uint32_t d, uint32_t a, int b_off, bool acc, int ch) {
         const uint32_t ba = v_lo + (b_off >> 4);
 #pragma unroll
-        for (int k = 0; k < kBlockN / 16; ++k)
+        for (int kk = 0; kk < 2; ++kk) {
+          const int k = 2 * ch + kk;
           umma_ts_w(tmem + d, tmem + a + k * 8, ba + ((k * 2048) >> 4), v_hi, idesc_ts, (acc || k > 0) ? 1u : 0u);
+        }
       };
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int b, h, idx, lo, hi;
@@ -232,15 +236,20 @@ __global__ void __launch_bounds__(192, 1)
           mma_ss(0, L::kOuter, in0);                // T0 = outer0 inner0^T
           mma_ss(128, L::kOuter + kTileBytes, in1);  // T1 = outer1 inner1^T
           tc_commit(bar(L::kSFull));
-          if (!mbar_wait(bar(L::kPFull), p_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
-          p_par ^= 1u;
-          tc_fence_after();
-          if (KV) {
-            mma_ts(256, 0, in1, n > lo);    // dV += P^T dO_i
-            mma_ts(384, 128, in0, n > lo);  // dK += dS^T Q_i
-          } else {
-            mma_ts(256, 128, in0, n > lo);  // dQ += dS K_j
+          // the accumulating MMAs of each 32-column chunk as soon as it is stored
+#pragma unroll 1
+          for (int ch = 0; ch < 4 && ok; ++ch) {
+            if (!mbar_wait(bar(L::kPFull + ch), p_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+            if (KV) {
+              mma_ts(256, 0, in1, n > lo, ch);    // dV += P^T dO_i
+              mma_ts(384, 128, in0, n > lo, ch);  // dK += dS^T Q_i
+            } else {
+              mma_ts(256, 128, in0, n > lo, ch);  // dQ += dS K_j
+            }
           }
+          if (!ok) break;
+          p_par ^= 1u;
           tc_commit(bar(L::kInEmpty + ring.stage));
           ring.advance<2>();
         }
@@ -335,14 +344,14 @@ __global__ void __launch_bounds__(192, 1)
             dk[c / 2] = pack_bf16x2(ds.x, ds.y);
           }
           // column chunk ch of P^T / dS^T (BF16 pairs) lands in columns [16 ch, 16 ch + 16),
-          // S / dP columns this thread has already read
+          // S / dP columns this thread has already read; the MMAs of the chunk may start
           if (KV) tmem_st16(tmem + lane_off + ch * 16, pk);
           tmem_st16(tmem + lane_off + 128 + ch * 16, dk);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(L::kPFull + ch));
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::kPFull));
       }
       if (!ok) break;
       // ------------------------------ epilogue ------------------------------
