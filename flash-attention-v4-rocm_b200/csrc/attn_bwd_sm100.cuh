@@ -41,6 +41,7 @@ struct BwdParams {
   __nv_bfloat16* g0;  // KV mode: dK, Q mode: dQ  ([B, S, H, 128])
   __nv_bfloat16* g1;  // KV mode: dV
   int batch, heads, sq, sk;
+  int stat_stride;    // row stride of lse2 / dsum (>= sq)
   float scale;        // softmax scale
   float scale_log2;   // scale * log2(e)
   int num_outer;      // outer tiles per (batch, head)
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(192, 1)
       const int o0 = idx * kBlockM;
       bwd_range<KV, Causal>(p, o0, lo, hi);
       const int mine = o0 + row;  // this thread's key (KV) or query row (Q)
-      const int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.sq;  // LSE / D row base
+      const int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.stat_stride;  // LSE / D row base
       // Q mode: this row's statistics (rows past Sq read row Sq-1 and are not stored)
       float2 lse2_row = make_float2(0.f, 0.f), d_row = make_float2(0.f, 0.f);
       if (!KV) {
@@ -413,11 +414,21 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// D = rowsum(dO * O) in FP32 and LSE * log2(e), one warp per (batch, row, head).
+// D = rowsum(dO * O) in FP32 and LSE * log2(e), one warp per (batch, row, head),
+// stored [B, H, stat_stride]; entries of rows sq .. stat_stride-1 are set to 0.
 __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o,
                                                             const __nv_bfloat16* __restrict__ dout,
                                                             const float* __restrict__ lse, float* __restrict__ dsum,
-                                                            float* __restrict__ lse2, int batch, int sq, int heads) {
+                                                            float* __restrict__ lse2, int batch, int sq, int heads,
+                                                            int stat_stride) {
+  const int pad = stat_stride - sq;
+  const int64_t pads = static_cast<int64_t>(batch) * heads * pad;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < pads;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t at = (t / pad) * stat_stride + sq + t % pad;
+    dsum[at] = 0.f;
+    lse2[at] = 0.f;
+  }
   const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
   const int lane = threadIdx.x % 32;
   for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < rows;
@@ -440,9 +451,9 @@ __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16*
       const int64_t br = w / heads;
       const int r = static_cast<int>(br % sq);
       const int64_t bb = br / sq;
-      const int64_t at = (bb * heads + h) * sq + r;
+      const int64_t at = (bb * heads + h) * stat_stride + r;  // padded statistics row
       dsum[at] = s;
-      lse2[at] = lse[at] * 1.4426950408889634f;
+      lse2[at] = lse[(bb * heads + h) * sq + r] * 1.4426950408889634f;  // the forward's LSE is [B, H, Sq]
     }
   }
 }

@@ -18,6 +18,7 @@
 
 #include "attn_fwd_sm100.cuh"
 #include "attn_bwd_sm100.cuh"
+#include "attn_bwd_fused_sm100.cuh"
 #include "combine.cuh"
 #include "tensor_map.h"
 #include "fav4_bshd.h"
@@ -609,8 +610,10 @@ extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, 
 }
 
 // --------------------------------------------------------------------------
-// Backward pass (no reference counterpart): D = rowsum(dO * O), then the KV
-// kernel (dK, dV) and the Q kernel (dQ), all on the caller's stream.
+// Backward pass (no reference counterpart), all on the caller's stream:
+// D = rowsum(dO * O), then either the fused kernel (dK, dV and FP32 dQ partial
+// sums by reduction, then the dQ conversion) or, deterministic, the KV kernel
+// (dK, dV) and the Q kernel (dQ).
 namespace fav4 {
 namespace {
 
@@ -654,6 +657,77 @@ int launch_bwd(const BwdParams& base, const CUtensorMap& o0, const CUtensorMap& 
   return cudaGetLastError();
 }
 
+template <bool Causal>
+int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const CUtensorMap& tq, const CUtensorMap& tdo, const DeviceInfo& info, int dev,
+                     cudaStream_t stream) {
+  auto kernel = attn_bwd_fused_kernel<Causal>;
+  constexpr int smem = BwdFusedSmem::kBytes;
+  {
+    static std::mutex mu;
+    static bool attr_set[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  BwdFusedParams p = base;
+  p.num_outer = (p.sk + kBlockN - 1) / kBlockN;
+  const int64_t tiles = static_cast<int64_t>(p.batch) * p.heads * p.num_outer;
+  if (tiles > INT_MAX) return cudaErrorInvalidValue;
+  p.num_tiles = static_cast<int>(tiles);
+  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  kernel<<<grid, 512, smem, stream>>>(tk, tv, tq, tdo, p);
+  return cudaGetLastError();
+}
+
+// Workspace: D and LSE * log2(e) as [B, H, q tiles * 128] (rows past Sq zero), then the
+// FP32 dQ accumulator [B, H, q tiles, 128, 128] (fused path only).
+size_t bwd_stat_bytes(const Fav4BwdArgs* a) {
+  const size_t nq = (static_cast<size_t>(a->sq) + kBlockM - 1) / kBlockM;
+  return round256(static_cast<size_t>(a->batch) * a->heads * nq * kBlockM * 4);
+}
+size_t bwd_acc_bytes(const Fav4BwdArgs* a) {
+  const size_t nq = (static_cast<size_t>(a->sq) + kBlockM - 1) / kBlockM;
+  return round256(static_cast<size_t>(a->batch) * a->heads * nq * kBlockM * kHeadDim * 4);
+}
+
+struct BwdSetup {
+  DeviceInfo info;
+  int dev = 0;
+  CUtensorMap tq, tk, tv, tdo;
+  float* dsum = nullptr;
+  float* lse2 = nullptr;
+  int stat_stride = 0;
+};
+
+// Validation, tensor maps and the preprocess (D, LSE * log2(e)) shared by both paths.
+int bwd_prepare(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                BwdSetup* st) {
+  if (!bwd_args_valid(a, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < fav4_bshd_backward_workspace_bytes(a))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaGetDevice(&st->dev);
+  if (e != cudaSuccess) return e;
+  if (!device_info(st->dev, &st->info)) return cudaErrorInvalidDevice;
+  if (!encode_bshd(&st->tq, a->q, a->batch, a->sq, a->heads) || !encode_bshd(&st->tk, a->k, a->batch, a->sk, a->heads) ||
+      !encode_bshd(&st->tv, a->v, a->batch, a->sk, a->heads) ||
+      !encode_bshd(&st->tdo, a->dout, a->batch, a->sq, a->heads))
+    return cudaErrorInvalidValue;
+  st->stat_stride = (a->sq + kBlockM - 1) / kBlockM * kBlockM;
+  st->dsum = static_cast<float*>(workspace);
+  st->lse2 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + bwd_stat_bytes(a));
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->sq * a->heads;
+  const int64_t want = (rows + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(st->info.sms) * 16;
+  attn_bwd_dsum_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, st->dsum,
+      st->lse2, a->batch, a->sq, a->heads, st->stat_stride);
+  return cudaGetLastError();
+}
+
 }  // namespace
 }  // namespace fav4
 
@@ -661,41 +735,59 @@ extern "C" size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* a) {
   if (!a || a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->batch > INT_MAX / a->heads ||
       a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128))
     return 0;
-  return 2 * fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4);  // D, LSE * log2(e)
+  return 2 * fav4::bwd_stat_bytes(a) + fav4::bwd_acc_bytes(a);
 }
 
 extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes,
                                   cudaStream_t stream) {
-  if (!fav4::bwd_args_valid(a, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
-      workspace_bytes < fav4_bshd_backward_workspace_bytes(a))
-    return cudaErrorInvalidValue;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  fav4::BwdSetup st;
+  cudaError_t e = static_cast<cudaError_t>(fav4::bwd_prepare(a, causal, workspace, workspace_bytes, stream, &st));
   if (e != cudaSuccess) return e;
-  fav4::DeviceInfo info;
-  if (!fav4::device_info(dev, &info)) return cudaErrorInvalidDevice;
-  CUtensorMap tq, tk, tv, tdo;
-  if (!fav4::encode_bshd(&tq, a->q, a->batch, a->sq, a->heads) ||
-      !fav4::encode_bshd(&tk, a->k, a->batch, a->sk, a->heads) ||
-      !fav4::encode_bshd(&tv, a->v, a->batch, a->sk, a->heads) ||
-      !fav4::encode_bshd(&tdo, a->dout, a->batch, a->sq, a->heads))
-    return cudaErrorInvalidValue;
-  float* dsum = static_cast<float*>(workspace);
-  float* lse2 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
-                                         fav4::round256(static_cast<size_t>(a->batch) * a->heads * a->sq * 4));
-  {
-    const int64_t rows = static_cast<int64_t>(a->batch) * a->sq * a->heads;
-    const int64_t want = (rows + 7) / 8;
-    const int64_t cap = static_cast<int64_t>(info.sms) * 16;
-    fav4::attn_bwd_dsum_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, dsum, lse2,
-        a->batch, a->sq, a->heads);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
+  float* acc = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 2 * fav4::bwd_stat_bytes(a));
+  const int nq = st.stat_stride / fav4::kBlockM;
+  e = cudaMemsetAsync(acc, 0, static_cast<size_t>(a->batch) * a->heads * nq * fav4::kBlockM * fav4::kHeadDim * 4,
+                      stream);
+  if (e != cudaSuccess) return e;
+  fav4::BwdFusedParams p = {};
+  p.lse2 = st.lse2;
+  p.dsum = st.dsum;
+  p.dq_acc = acc;
+  p.dk = static_cast<__nv_bfloat16*>(a->dk);
+  p.dv = static_cast<__nv_bfloat16*>(a->dv);
+  p.batch = a->batch;
+  p.heads = a->heads;
+  p.sq = a->sq;
+  p.sk = a->sk;
+  p.stat_stride = st.stat_stride;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.status = st.info.status;
+  p.wait_limit_ns = fav4::wait_limit_ns();
+  e = static_cast<cudaError_t>(causal ? fav4::launch_bwd_fused<true>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream)
+                                      : fav4::launch_bwd_fused<false>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream));
+  if (e != cudaSuccess) return e;
+  const int64_t threads = static_cast<int64_t>(a->batch) * a->heads * nq * fav4::kBlockM * 4;
+  const int64_t want = (threads + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(st.info.sms) * 16;
+  fav4::attn_bwd_dq_convert_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
+      acc, static_cast<__nv_bfloat16*>(a->dq), a->batch, a->heads, a->sq, a->scale);
+  return cudaGetLastError();
+}
+
+extern "C" int fav4_bshd_backward_deterministic(const Fav4BwdArgs* a, int causal, void* workspace,
+                                                size_t workspace_bytes, cudaStream_t stream) {
+  fav4::BwdSetup st;
+  cudaError_t e = static_cast<cudaError_t>(fav4::bwd_prepare(a, causal, workspace, workspace_bytes, stream, &st));
+  if (e != cudaSuccess) return e;
+  const fav4::DeviceInfo& info = st.info;
+  const int dev = st.dev;
+  const CUtensorMap &tq = st.tq, &tk = st.tk, &tv = st.tv, &tdo = st.tdo;
+  float* dsum = st.dsum;
+  float* lse2 = st.lse2;
   fav4::BwdParams p = {};
   p.lse2 = lse2;
   p.dsum = dsum;
+  p.stat_stride = st.stat_stride;
   p.batch = a->batch;
   p.heads = a->heads;
   p.sq = a->sq;

@@ -21,6 +21,7 @@ enum : uint32_t {
   kStatusTimeoutSoftmax = 4u,  // softmax warps gave up waiting for S / O
   kStatusTimeoutDrain = 8u,    // teardown gave up draining in-flight copies
   kStatusTimeoutProbe = 16u,   // probe kernel wait ran out (tests only)
+  kStatusSmemAlign = 32u,      // dynamic shared memory not 1 KiB aligned (kernel did nothing)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

@@ -85,6 +85,8 @@ def _bind(lib):
     lib.fav4_bshd_backward_workspace_bytes.restype = C.c_size_t
     lib.fav4_bshd_backward.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.fav4_bshd_backward.restype = C.c_int
+    lib.fav4_bshd_backward_deterministic.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.fav4_bshd_backward_deterministic.restype = C.c_int
     lib.fav4_bshd_forward_varlen.argtypes = [C.POINTER(VarlenArgs), C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_varlen.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
@@ -294,10 +296,10 @@ class Runner:
         if status:
             raise RuntimeError(f"varlen config {config}: CUDA status {status}")
 
-    def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None):
-        """dQ, dK, dV through fav4_bshd_backward (all BF16 BSHD CUDA tensors,
-        lse the forward's FP32 [B, H, Sq]). The D workspace is allocated with
-        torch and kept for the next call of the same shape."""
+    def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None, deterministic=False):
+        """dQ, dK, dV through fav4_bshd_backward, or fav4_bshd_backward_deterministic
+        (all BF16 BSHD CUDA tensors, lse the forward's FP32 [B, H, Sq]). The
+        workspace is allocated with torch and kept for the next call."""
         import torch
         for x in (q, k, v, o, dout, dq, dk, dv):
             assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
@@ -311,7 +313,8 @@ class Runner:
         ws = getattr(self, "_bwd_ws", None)
         if ws is None or ws.numel() < need or ws.device != q.device:
             ws = self._bwd_ws = torch.empty(need, dtype=torch.uint8, device=q.device)
-        status = self.lib.fav4_bshd_backward(C.byref(a), int(causal), ws.data_ptr(), ws.numel(), _stream(stream))
+        fn = self.lib.fav4_bshd_backward_deterministic if deterministic else self.lib.fav4_bshd_backward
+        status = fn(C.byref(a), int(causal), ws.data_ptr(), ws.numel(), _stream(stream))
         if status:
             raise RuntimeError(f"backward: CUDA status {status}")
 

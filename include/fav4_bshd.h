@@ -171,19 +171,30 @@ struct Fav4BwdArgs {
 };
 typedef struct Fav4BwdArgs Fav4BwdArgs;
 
-/* Device workspace fav4_bshd_backward needs (D = rowsum(dO * O) and
- * LSE * log2(e), FP32 [batch, heads, sq] each); 0 on invalid arguments. */
+/* Device workspace fav4_bshd_backward and fav4_bshd_backward_deterministic
+ * need: D = rowsum(dO * O) and LSE * log2(e) (FP32 [batch, heads, q tiles *
+ * 128] each) and the FP32 dQ accumulator (batch * heads * q tiles * 128 * 128
+ * floats), q tiles = ceil(sq / 128); 0 on invalid arguments. */
 size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* args);
 
-/* dQ, dK, dV of O = softmax(Q K^T * scale) V (causal: top-left). Three
- * kernels on `stream`: D, then dK/dV (work tiles of 128 keys), then dQ (work
- * tiles of 128 query rows); no atomics, deterministic. Same mask convention
- * as fav4_bshd_forward; keys no query row sees get zero gradients. workspace:
- * device memory, 256-byte aligned, fav4_bshd_backward_workspace_bytes long.
- * Returns 0, cudaErrorInvalidValue (1) on invalid arguments, else the first
- * failing launch status. */
+/* dQ, dK, dV of O = softmax(Q K^T * scale) V (causal: top-left). On
+ * `stream`: D, a zero fill of the dQ accumulator, one fused kernel (work
+ * tiles of 128 keys: dK and dV, and each key tile's dQ contribution added
+ * into the FP32 accumulator by atomic reductions), then the BF16 conversion
+ * of dQ. dK and dV are deterministic; dQ's FP32 summation order is not.
+ * Same mask convention as fav4_bshd_forward; keys no query row sees get zero
+ * gradients. workspace: device memory, 256-byte aligned,
+ * fav4_bshd_backward_workspace_bytes long. Returns 0, cudaErrorInvalidValue
+ * (1) on invalid arguments, else the first failing launch status. */
 int fav4_bshd_backward(const Fav4BwdArgs* args, int causal, void* workspace, size_t workspace_bytes,
                        cudaStream_t stream);
+
+/* The same gradients with no atomics, bit-reproducible run to run: D, then
+ * dK/dV (work tiles of 128 keys), then dQ (work tiles of 128 query rows,
+ * recomputing S and dP). Slower than fav4_bshd_backward. Same arguments,
+ * workspace and return values. */
+int fav4_bshd_backward_deterministic(const Fav4BwdArgs* args, int causal, void* workspace,
+                                     size_t workspace_bytes, cudaStream_t stream);
 
 /* One output of fav4_bshd_forward_host: host buffers for O (BF16
  * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and

@@ -223,17 +223,20 @@ def test_backward_rejects_invalid_arguments(lib):
                          a["heads"], a["sq"], a["sk"], a["scale"])
     good = bwd()
     need = lib.fav4_bshd_backward_workspace_bytes(C.byref(good))
-    assert need == 2 * ((2 * 4 * 64 * 4 + 255) // 256 * 256)
+    # D and LSE * log2(e) over one padded query tile, then the FP32 dQ accumulator
+    assert need == 2 * (2 * 4 * 128 * 4) + 2 * 4 * 128 * 128 * 4
+    assert lib.fav4_bshd_backward_workspace_bytes(C.byref(bwd(sq=129))) == 2 * (need - 2 * (2 * 4 * 128 * 4)) + \
+        2 * (2 * 2 * 4 * 128 * 4)
     ws = A16 * 256
-    f = lib.fav4_bshd_backward
-    for kw in (dict(q=None), dict(dout=None), dict(lse=None), dict(dk=None), dict(batch=0), dict(sk=0),
-               dict(scale=0.0), dict(scale=float("nan")), dict(dq=A16 + 8), dict(lse=A16 + 2),
-               dict(heads=2 ** 24 + 1)):
-        assert f(C.byref(bwd(**kw)), 0, ws, need, None) == INVALID, kw
-    assert f(C.byref(good), 2, ws, need, None) == INVALID        # bad mode
-    assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
-    assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
-    assert f(C.byref(good), 0, None, need, None) == INVALID
+    for f in (lib.fav4_bshd_backward, lib.fav4_bshd_backward_deterministic):
+        for kw in (dict(q=None), dict(dout=None), dict(lse=None), dict(dk=None), dict(batch=0), dict(sk=0),
+                   dict(scale=0.0), dict(scale=float("nan")), dict(dq=A16 + 8), dict(lse=A16 + 2),
+                   dict(heads=2 ** 24 + 1)):
+            assert f(C.byref(bwd(**kw)), 0, ws, need, None) == INVALID, kw
+        assert f(C.byref(good), 2, ws, need, None) == INVALID        # bad mode
+        assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
+        assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
+        assert f(C.byref(good), 0, None, need, None) == INVALID
 
 
 def test_varlen_rejects_invalid_arguments(lib):

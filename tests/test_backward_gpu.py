@@ -1,7 +1,9 @@
-"""GPU tests of the backward pass (fav4_bshd_backward): dQ, dK, dV against
+"""GPU tests of the backward pass (fav4_bshd_backward, the fused kernel with
+FP32 dQ reductions, and fav4_bshd_backward_deterministic): dQ, dK, dV against
 torch autograd in FP32 on the GPU (same BF16 inputs) and against the FP64
 oracle on small cases, dense and top-left causal, ragged shapes, Sq != Sk;
-determinism; keys no query row sees get zero gradients."""
+run-to-run reproducibility of the deterministic path; dK and dV of both paths
+bit-identical; keys no query row sees get zero gradients."""
 import math
 
 import numpy as np
@@ -21,13 +23,13 @@ def _inputs(b, h, sq, sk, seed):
     return q, k, v, do
 
 
-def _run(runner, q, k, v, do, causal, scale):
+def _run(runner, q, k, v, do, causal, scale, deterministic=False):
     b, sq, h, _ = q.shape
     o = torch.empty_like(q)
     lse = torch.empty((b, h, sq), device="cuda")
     runner.call(q, k, v, o, lse, causal, 0, scale)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    runner.backward(q, k, v, o, do, lse, dq, dk, dv, causal, scale)
+    runner.backward(q, k, v, o, do, lse, dq, dk, dv, causal, scale, deterministic=deterministic)
     torch.cuda.synchronize()
     return dq, dk, dv
 
@@ -54,10 +56,11 @@ def _check(got, want, name):
 @pytest.mark.parametrize("b,h,sq,sk", [(1, 2, 128, 128), (2, 3, 300, 517), (1, 2, 1000, 1537), (2, 2, 1537, 1000),
                                        (1, 4, 64, 2000), (2, 2, 257, 1), (1, 8, 2048, 2048)])
 @pytest.mark.parametrize("causal", [False, True])
-def test_backward_matches_torch_autograd(runner, b, h, sq, sk, causal):
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_backward_matches_torch_autograd(runner, b, h, sq, sk, causal, deterministic):
     q, k, v, do = _inputs(b, h, sq, sk, seed=sq + sk)
     scale = 1 / math.sqrt(128)
-    got = _run(runner, q, k, v, do, causal, scale)
+    got = _run(runner, q, k, v, do, causal, scale, deterministic)
     want = _torch_grads(q, k, v, do, causal, scale)
     for g, w, n in zip(got, want, ("dq", "dk", "dv")):
         _check(g, w, n)
@@ -68,17 +71,30 @@ def test_backward_matches_torch_autograd(runner, b, h, sq, sk, causal):
 
 
 @pytest.mark.parametrize("causal", [False, True])
-def test_backward_against_fp64_oracle(runner, causal):
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_backward_against_fp64_oracle(runner, causal, deterministic):
     q, k, v, do = _inputs(1, 2, 200, 333, seed=5)
     scale = 0.09
-    got = _run(runner, q, k, v, do, causal, scale)
+    got = _run(runner, q, k, v, do, causal, scale, deterministic)
     dq, dk, dv, _, _ = R.reference_backward(*(x.float().cpu().numpy() for x in (q, k, v, do)), causal, scale)
     for g, w, n in zip(got, (dq, dk, dv), ("dq", "dk", "dv")):
         _check(g, torch.tensor(w, device="cuda", dtype=torch.float32), n)
 
 
-def test_backward_is_deterministic(runner):
+def test_backward_deterministic_is_reproducible(runner):
     q, k, v, do = _inputs(2, 4, 700, 700, seed=9)
-    a = _run(runner, q, k, v, do, True, 0.08)
-    b = _run(runner, q, k, v, do, True, 0.08)
+    a = _run(runner, q, k, v, do, True, 0.08, deterministic=True)
+    b = _run(runner, q, k, v, do, True, 0.08, deterministic=True)
     assert all(torch.equal(x, y) for x, y in zip(a, b))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_dk_dv_match_deterministic_bitwise(runner, causal):
+    # same elementwise arithmetic and MMA order for dK, dV; only dQ's summation order differs
+    q, k, v, do = _inputs(2, 3, 700, 900, seed=11)
+    fused = _run(runner, q, k, v, do, causal, 0.08)
+    det = _run(runner, q, k, v, do, causal, 0.08, deterministic=True)
+    assert torch.equal(fused[1], det[1]) and torch.equal(fused[2], det[2])
+    err = (fused[0].float() - det[0].float()).abs().max().item()
+    assert err <= 0.01 * det[0].float().abs().max().item() + 1e-3, err
+    assert runner.pipeline_status() == 0
