@@ -10,6 +10,10 @@
 //   dV += P^T dO_i           dK += dS^T Q_i                    (TMEM, whole loop)
 //   dQ_i(j) = dS K_j                                           (TMEM, per step)
 //
+// dS goes to shared memory once, keys as rows and queries contiguous (128-byte
+// swizzle, two 64-query boxes): the K-major A operand of dK = dS^T Q_i and the
+// MN-major A operand of dQ = dS K_j.
+//
 // and adds dQ_i(j) into an FP32 accumulator with vector reductions
 // (`red.global.add.v4.f32`); a separate pass scales and converts the
 // accumulator to BF16. Five GEMMs per (i, j) pair, one exponential pass.
@@ -23,11 +27,10 @@
 //   warp 12     TMA producer. warp 13: one thread issues every MMA and owns
 //               TMEM. warps 14-15 idle.
 //
-// TMEM (512 columns): T0 = S^T, T1 = dP^T, T2 = dV, T3 = dK. P^T and dS^T
-// (BF16 pairs) overwrite, for the query half h, columns [64 h, 64 h + 32) of
-// T0 / T1: columns that only that half's warps read. dQ_i(j) reuses all of T1
-// once dK has read dS^T. dS also goes to shared memory in the MN-major
-// 128-byte-swizzle layout, as the A operand of the dQ MMA (B = K_j, MN-major).
+// TMEM (512 columns): T0 = S^T, T1 = dP^T, T2 = dV, T3 = dK. P^T (BF16 pairs)
+// overwrites, for the query half h, columns [64 h, 64 h + 32) of T0: columns
+// that only that half's warps read. dQ_i(j) reuses all of T1 once the
+// elementwise warps have read dP^T.
 //
 // Issue order for step i (one thread, so the tensor pipe runs it in order):
 //   dV(i)  S^T(i+1)  dK(i)  dQ(i)  [the drain has read dQ(i)]  dP^T(i+1)
@@ -75,7 +78,8 @@ struct BwdFusedSmem {
 };
 
 // Register split: elementwise warpgroups, drain warpgroup, TMA/MMA warpgroup.
-constexpr uint32_t kBwdLaunchRegs = 128, kBwdElemRegs = 152, kBwdDrainRegs = 144, kBwdOtherRegs = 64;
+// (88 for the TMA/MMA warpgroup: with fewer the MMA issue loop spills to local memory.)
+constexpr uint32_t kBwdLaunchRegs = 128, kBwdElemRegs = 144, kBwdDrainRegs = 136, kBwdOtherRegs = 88;
 static_assert(128 * (2 * kBwdElemRegs + kBwdDrainRegs + kBwdOtherRegs) <= 512 * kBwdLaunchRegs,
               "register split exceeds the launch");
 static_assert(kBwdElemRegs > kBwdLaunchRegs && kBwdDrainRegs > kBwdLaunchRegs && kBwdOtherRegs < kBwdLaunchRegs,
@@ -213,6 +217,7 @@ __global__ void __launch_bounds__(512, 1)
       constexpr uint32_t idesc_ss = make_idesc_bf16(kBlockM, kBlockN, false);              // A, B K-major
       constexpr uint32_t idesc_ts = make_idesc_bf16(kBlockM, kHeadDim, true);              // A TMEM, B MN-major
       constexpr uint32_t idesc_dq = make_idesc_bf16(kBlockM, kHeadDim, true) | (1u << 15);  // A, B MN-major
+      constexpr uint32_t idesc_dk = make_idesc_bf16(kBlockN, kHeadDim, true);               // A K-major, B MN-major
       const uint64_t dk = make_sdesc_sw128(sbase, 16, 1024);
       const uint64_t dv = make_sdesc_sw128(sbase, kBoxBytes, 1024);
       const uint32_t k_lo = static_cast<uint32_t>(dk), k_hi = static_cast<uint32_t>(dk >> 32);
@@ -237,6 +242,13 @@ __global__ void __launch_bounds__(512, 1)
         for (int k = 0; k < kBlockM / 16; ++k)
           umma_ts_w(tmem + d, tmem + a + k * 8 + (k >= 4 ? 32 : 0), ba + ((k * 2048) >> 4), v_hi, idesc_ts,
                     (acc || k > 0) ? 1u : 0u);
+      };
+      // T3 += dS^T Q_i over the 128 queries: A = dS (K-major: keys as rows), B = Q_i (MN-major)
+      auto mma_dk = [&](int q_off, bool acc) {
+#pragma unroll
+        for (int k = 0; k < kBlockM / 16; ++k)
+          umma_ss_w(tmem + 384, k_lo + ((L::kDS + (k / 4) * kBoxBytes + (k % 4) * 32) >> 4), k_hi,
+                    v_lo + ((q_off + k * 2048) >> 4), v_hi, idesc_dk, (acc || k > 0) ? 1u : 0u);
       };
       // T1 = dS K_j over the 128 keys: A = dS (MN-major, queries contiguous), B = K_j (MN-major)
       auto mma_dq = [&]() {
@@ -284,9 +296,9 @@ __global__ void __launch_bounds__(512, 1)
           if (!mbar_wait(bar(L::kDSFull), ds_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
           ds_par ^= 1u;
           tc_fence_after();
-          mma_ts(384, 128, L::kQ + cur * kTileBytes, i > lo);  // dK += dS^T Q_i
-          tc_commit(bar(L::kInEmpty + cur));                   // Q_i, dO_i read for the last time
-          mma_dq();                                            // T1 = dS K_j, after dK has read dS^T
+          mma_dk(L::kQ + cur * kTileBytes, i > lo);  // dK += dS^T Q_i
+          tc_commit(bar(L::kInEmpty + cur));         // Q_i, dO_i read for the last time
+          mma_dq();                                  // T1 = dS K_j
           tc_commit(bar(L::kDQFull));
           if (more) {
             if (!mbar_wait(bar(L::kDQEmpty), dq_empty_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
@@ -397,7 +409,7 @@ __global__ void __launch_bounds__(512, 1)
     const int key_lane = (warp % 4) * 32 + lane;  // TMEM lane = key within the tile
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
     const uint32_t t_s = tmem + lane_off + half * 64;        // this half's S^T columns; P^T at +0..31
-    const uint32_t t_dp = tmem + lane_off + 128 + half * 64;  // dP^T; dS^T at +0..31
+    const uint32_t t_dp = tmem + lane_off + 128 + half * 64;  // dP^T
     // dS row of this key in the MN-major A tile: box `half`, 128 bytes per key, 16-byte chunks swizzled
     uint8_t* ds_row = smem + L::kDS + half * kBoxBytes + key_lane * 128;
     const int sw = key_lane & 7;
@@ -453,7 +465,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::kPFull));
-        // ---- phase B: dS^T = P^T (dP^T - D) -> TMEM (dK) and shared memory (dQ) ----
+        // ---- phase B: dS^T = P^T (dP^T - D) -> shared memory (dK, dQ) ----
         if (!warp_wait(bar(L::kDPFull), dp_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         dp_par ^= 1u;
         tc_fence_after();
@@ -475,7 +487,6 @@ __global__ void __launch_bounds__(512, 1)
             dk[e / 2] = pack_bf16x2(sa.x, sa.y);
             dk[e / 2 + 1] = pack_bf16x2(sb.x, sb.y);
           }
-          tmem_st16(t_dp + c * 16, dk);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int chunk = c * 4 + j;  // 8 queries per 16-byte chunk
@@ -483,9 +494,8 @@ __global__ void __launch_bounds__(512, 1)
                 make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
           }
         }
-        tmem_st_wait();
         fence_proxy_async_smem();  // dS visible to the tensor core
-        tc_fence_before();
+        tc_fence_before();         // dP^T reads done: T1 may take dQ
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(bar(L::kDSFull));
