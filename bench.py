@@ -353,9 +353,10 @@ def run_compare(args):
 def run_backward(args):
     """Backward pass, one GPU: B H S of the headline (or --batch/--seq), dense
     and causal. FLOPs by the usual convention, 2.5x the forward's (five
-    matmuls: dV, dP, dQ, dK and the recomputed S); this library computes seven
-    (S and dP in both the dK/dV and the dQ kernels). torch SDPA's cuDNN
-    backward on the same tensors is timed beside it. One JSON line per mask."""
+    matmuls: dV, dP, dQ, dK and the recomputed S). fav4_bshd_backward (the
+    fused kernel, five matmuls) is the timed path; the deterministic two-kernel
+    path (seven matmuls) and torch SDPA's cuDNN backward on the same tensors
+    are timed beside it. One JSON line per mask."""
     import torch
     import torch.nn.functional as Fn
     from torch.nn.attention import SDPBackend, sdpa_kernel
@@ -390,6 +391,9 @@ def run_backward(args):
                 "tflops": f / (ms * 1e-3) / 1e12, "frac_of_measured_bf16": f / (ms * 1e-3) / 1e12 / pk["bf16_tflops"],
                 "peak_source": pk_kind, "flop_convention": "2.5 x forward (5 matmuls)",
                 "pipeline_status": runner.pipeline_status(clear=True)}
+        dms = timed(lambda: runner.backward(q, k, v, o, do, lse, dq, dk, dv, causal, scale, deterministic=True))
+        line["deterministic_ms"] = dms
+        line["deterministic_tflops"] = f / (dms * 1e-3) / 1e12
         try:
             tq, tk, tv = (x.transpose(1, 2).detach().requires_grad_(True) for x in (q, k, v))
             tdo = do.transpose(1, 2)

@@ -82,8 +82,9 @@ def test_gradients_through_the_operator(runner):
     runner.backward(q, k, v, o2, do, lse, dq, dk, dv, True, 1 / math.sqrt(128))
     torch.cuda.synchronize()
     assert torch.equal(o.detach(), o2)
-    assert torch.equal(qg.grad, dq) and torch.equal(kg.grad, dk) and torch.equal(vg.grad, vg.grad)
-    assert torch.equal(vg.grad, dv)
+    assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
+    # dQ is summed by FP32 atomic reductions: the order, and so the last bit, may differ between runs
+    assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
 
 
 def test_gradient_limits_raise():
