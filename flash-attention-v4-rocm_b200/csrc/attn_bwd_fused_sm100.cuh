@@ -1,9 +1,11 @@
 // Fused BF16 attention backward for B200 (sm_100a): dK, dV and the dQ
 // partial sums of one key tile in a single pass over the query tiles.
 //
-// A work tile is (batch, head, 128 keys). K_j and V_j stay in shared memory;
-// for every query tile i that sees them (Q_i, dO_i and the tile's LSE*log2(e)
-// and D rows arrive by TMA in a two-stage ring) the kernel computes
+// A work tile is (batch, K/V head, 128 keys). K_j and V_j stay in shared
+// memory; for every query head of the K/V head's group (one head without
+// grouped-query attention) and every query tile i that sees them (Q_i, dO_i
+// and the tile's LSE*log2(e) and D rows arrive by TMA in a two-stage ring)
+// the kernel computes
 //
 //   S^T = K_j Q_i^T          dP^T = V_j dO_i^T                 (TMEM)
 //   P^T = exp2(S^T scale log2e - LSE2)   dS^T = P^T (dP^T - D)  (registers)
@@ -45,13 +47,14 @@ struct BwdFusedParams {
   const float* lse2;  // LSE * log2(e), [B, H, stat_stride] (rows past Sq are 0)
   const float* dsum;  // D = rowsum(dO * O), same layout
   float* dq_acc;      // [B, H, q tiles, 32 column quads, 128 rows, 4] FP32, zeroed before the launch
-  __nv_bfloat16* dk;  // [B, Sk, H, 128]
+  __nv_bfloat16* dk;  // [B, Sk, H_kv, 128]
   __nv_bfloat16* dv;
   int batch, heads, sq, sk;
+  int kv_heads, group;  // K/V heads, heads / kv_heads
   int stat_stride;    // q tiles * 128
   float scale, scale_log2;
   int num_outer;      // key tiles per (batch, head)
-  int num_tiles;      // batch * heads * num_outer
+  int num_tiles;      // batch * kv_heads * num_outer
   uint32_t* status;
   uint64_t wait_limit_ns;
 };
@@ -116,10 +119,12 @@ __global__ void __launch_bounds__(512, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   WaitCtl ctl{abort_flag, p.status, p.wait_limit_ns};
-  BwdParams rp = {};  // the fields bwd_range / bwd_tile read
+  BwdParams rp = {};  // the fields bwd_range / bwd_tile / bwd_step read
   rp.sq = p.sq;
   rp.sk = p.sk;
   rp.heads = p.heads;
+  rp.kv_heads = p.kv_heads;
+  rp.group = p.group;
   rp.num_outer = p.num_outer;
 
   if (threadIdx.x == 0) {
@@ -181,8 +186,11 @@ __global__ void __launch_bounds__(512, 1)
           tma_load_4d(sbase + L::kK + c * kBoxBytes, &tm_k, bar(L::kKVFull), c * 64, h, o0, b, pol);
           tma_load_4d(sbase + L::kV + c * kBoxBytes, &tm_v, bar(L::kKVFull), c * 64, h, o0, b, pol);
         }
-        const int64_t stat_bh = (static_cast<int64_t>(b) * p.heads + h) * p.stat_stride;
-        for (int i = lo; i < hi && ok; ++i) {
+        const int steps = bwd_steps<true>(rp, lo, hi);
+        for (int st = 0; st < steps && ok; ++st) {
+          int hq, i;
+          bwd_step<true>(rp, h, lo, hi, st, hq, i);
+          const int64_t stat_bh = (static_cast<int64_t>(b) * p.heads + hq) * p.stat_stride;
           if (!mbar_wait(bar(L::kInEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
             ok = false;
             break;
@@ -193,13 +201,13 @@ __global__ void __launch_bounds__(512, 1)
           armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
           const int row = i * kBlockM;
           for (int c = 0; c < 2; ++c) {
-            tma_load_4d(sbase + L::kQ + ring.stage * kTileBytes + c * kBoxBytes, &tm_q, fb, c * 64, h, row, b, pol);
-            tma_load_4d(sbase + L::kDO + ring.stage * kTileBytes + c * kBoxBytes, &tm_do, fb, c * 64, h, row, b,
+            tma_load_4d(sbase + L::kQ + ring.stage * kTileBytes + c * kBoxBytes, &tm_q, fb, c * 64, hq, row, b, pol);
+            tma_load_4d(sbase + L::kDO + ring.stage * kTileBytes + c * kBoxBytes, &tm_do, fb, c * 64, hq, row, b,
                         pol);
           }
-          const uint32_t st = sbase + L::kStat + ring.stage * L::kStatBytes;
-          bulk_load(st, p.lse2 + stat_bh + row, kBlockM * 4, fb);
-          bulk_load(st + kBlockM * 4, p.dsum + stat_bh + row, kBlockM * 4, fb);
+          const uint32_t sa = sbase + L::kStat + ring.stage * L::kStatBytes;
+          bulk_load(sa, p.lse2 + stat_bh + row, kBlockM * 4, fb);
+          bulk_load(sa + kBlockM * 4, p.dsum + stat_bh + row, kBlockM * 4, fb);
           ring.advance<2>();
         }
       }
@@ -273,19 +281,20 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         mma_ss(128, L::kV, L::kDO + ring.stage * kTileBytes);  // dP^T(lo)
         tc_commit(bar(L::kDPFull));
-        for (int i = lo; i < hi && ok; ++i) {
+        const int steps = bwd_steps<true>(rp, lo, hi);
+        for (int st = 0; st < steps && ok; ++st) {
           const int cur = ring.stage;
           Ring nxt = ring;
           nxt.advance<2>();
-          const bool more = i + 1 < hi;
+          const bool more = st + 1 < steps;
           if (!mbar_wait(bar(L::kPFull), p_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
           p_par ^= 1u;
-          if (i == lo) {
+          if (st == 0) {
             if (!mbar_wait(bar(L::kAccEmpty), acc_empty_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
             acc_empty_par ^= 1u;
           }
           tc_fence_after();
-          mma_ts(256, 0, L::kDO + cur * kTileBytes, i > lo);  // dV += P^T dO_i
+          mma_ts(256, 0, L::kDO + cur * kTileBytes, st > 0);  // dV += P^T dO_i
           if (more) {
             // S^T(i+1) overwrites T0 after dV has read P^T(i) (same thread, issue order)
             if (!mbar_wait(bar(L::kInFull + nxt.stage), nxt.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
@@ -296,7 +305,7 @@ __global__ void __launch_bounds__(512, 1)
           if (!mbar_wait(bar(L::kDSFull), ds_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
           ds_par ^= 1u;
           tc_fence_after();
-          mma_dk(L::kQ + cur * kTileBytes, i > lo);  // dK += dS^T Q_i
+          mma_dk(L::kQ + cur * kTileBytes, st > 0);  // dK += dS^T Q_i
           tc_commit(bar(L::kInEmpty + cur));         // Q_i, dO_i read for the last time
           mma_dq();                                  // T1 = dS K_j
           tc_commit(bar(L::kDQFull));
@@ -333,7 +342,10 @@ __global__ void __launch_bounds__(512, 1)
       const int o0 = idx * kBlockN;
       bwd_range<true, Causal>(rp, o0, lo, hi);
       const int key = o0 + row;
-      for (int i = lo; i < hi; ++i) {
+      const int steps = bwd_steps<true>(rp, lo, hi);
+      for (int st = 0; st < steps; ++st) {
+        int hq, i;
+        bwd_step<true>(rp, h, lo, hi, st, hq, i);
         if (!warp_wait(bar(L::kDQFull), dq_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         dq_par ^= 1u;
         tc_fence_after();
@@ -346,7 +358,7 @@ __global__ void __launch_bounds__(512, 1)
         if (lane == 0) mbar_arrive(bar(L::kDQEmpty));  // T1 may take dP^T(i+1)
         // tile (b, h, i) of the accumulator: [32 column quads][128 rows][4]; a warp's reduction
         // covers 32 consecutive rows of one quad, 512 contiguous bytes
-        float* acc = p.dq_acc + ((static_cast<int64_t>(b) * p.heads + h) * nq + i) * (kBlockM * kHeadDim) + row * 4;
+        float* acc = p.dq_acc + ((static_cast<int64_t>(b) * p.heads + hq) * nq + i) * (kBlockM * kHeadDim) + row * 4;
 #pragma unroll
         for (int q4 = 0; q4 < 32; ++q4) {
           const uint32_t* s = &v[q4 / 8][(q4 % 8) * 4];
@@ -358,7 +370,7 @@ __global__ void __launch_bounds__(512, 1)
       if (hi <= lo) {
         // no query row sees these keys (causal, Sk > Sq): zero gradients
         if (key < p.sk) {
-          const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.heads + h) * kHeadDim;
+          const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.kv_heads + h) * kHeadDim;
           uint4* d0 = reinterpret_cast<uint4*>(p.dk + off);
           uint4* d1 = reinterpret_cast<uint4*>(p.dv + off);
 #pragma unroll
@@ -372,7 +384,7 @@ __global__ void __launch_bounds__(512, 1)
       if (!warp_wait(bar(L::kAccFull), acc_full_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
       acc_full_par ^= 1u;
       tc_fence_after();
-      const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.heads + h) * kHeadDim;
+      const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.kv_heads + h) * kHeadDim;
 #pragma unroll 1
       for (int g = 0; g < 2; ++g) {
         // g = 0: dK (T3, times scale); g = 1: dV (T2)
@@ -423,7 +435,10 @@ __global__ void __launch_bounds__(512, 1)
       const int o0 = idx * kBlockN;
       bwd_range<true, Causal>(rp, o0, lo, hi);
       const int key = o0 + key_lane;
-      for (int i = lo; i < hi; ++i) {
+      const int steps = bwd_steps<true>(rp, lo, hi);
+      for (int st = 0; st < steps; ++st) {
+        int hq, i;
+        bwd_step<true>(rp, h, lo, hi, st, hq, i);
         const float* stat = reinterpret_cast<const float*>(smem + L::kStat + ring.stage * L::kStatBytes);
         if (!warp_wait(bar(L::kInFull + ring.stage), ring.phase, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         if (!warp_wait(bar(L::kSFull), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }

@@ -41,11 +41,13 @@ struct BwdParams {
   __nv_bfloat16* g0;  // KV mode: dK, Q mode: dQ  ([B, S, H, 128])
   __nv_bfloat16* g1;  // KV mode: dV
   int batch, heads, sq, sk;
+  int kv_heads;       // K / V heads (a divisor of heads: grouped-query attention)
+  int group;          // heads / kv_heads
   int stat_stride;    // row stride of lse2 / dsum (>= sq)
   float scale;        // softmax scale
   float scale_log2;   // scale * log2(e)
   int num_outer;      // outer tiles per (batch, head)
-  int num_tiles;      // batch * heads * num_outer
+  int num_tiles;      // batch * (KV mode: kv_heads, Q mode: heads) * num_outer
   uint32_t* status;
   uint64_t wait_limit_ns;
 };
@@ -79,15 +81,37 @@ __device__ __forceinline__ void bwd_range(const BwdParams& p, int o0, int& lo, i
   }
 }
 
+// Work tile t: batch b, head h (KV mode: a K / V head, Q mode: a query head), outer tile idx.
 template <bool Causal>
 __device__ __forceinline__ void bwd_tile(const BwdParams& p, int t, int& b, int& h, int& idx, bool kv) {
-  const int per_batch = p.heads * p.num_outer;
+  const int th = kv ? p.kv_heads : p.heads;
+  const int per_batch = th * p.num_outer;
   b = t / per_batch;
   const int w = t - b * per_batch;
-  h = w % p.heads;
-  const int k = w / p.heads;
+  h = w % th;
+  const int k = w / th;
   // causal: the longest loops first (low key tiles in KV mode, high row tiles in Q mode)
   idx = (Causal && !kv) ? p.num_outer - 1 - k : k;
+}
+
+// Inner steps of a work tile. KV mode walks the query tiles [lo, hi) of each
+// query head of the K / V head's group in turn (dK, dV sum over the group);
+// Q mode walks the key tiles [lo, hi).
+template <bool KV>
+__device__ __forceinline__ int bwd_steps(const BwdParams& p, int lo, int hi) {
+  return KV ? (hi - lo) * p.group : hi - lo;
+}
+// Step s: the query head hq of the inner tile and the inner tile index n.
+template <bool KV>
+__device__ __forceinline__ void bwd_step(const BwdParams& p, int h, int lo, int hi, int s, int& hq, int& n) {
+  if (KV) {
+    const int len = hi - lo;
+    hq = h * p.group + s / len;
+    n = lo + s % len;
+  } else {
+    hq = h;
+    n = lo + s;
+  }
 }
 
 template <bool KV, bool Causal>
@@ -161,7 +185,11 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_4d(sbase + L::kOuter + kTileBytes + c * kBoxBytes, &tm_o1, bar(L::kOuterFull), c * 64, h, o0, b,
                       pol);
         }
-        for (int n = lo; n < hi && ok; ++n) {
+        const int steps = bwd_steps<KV>(p, lo, hi);
+        for (int st = 0; st < steps && ok; ++st) {
+          int hq, n;
+          bwd_step<KV>(p, h, lo, hi, st, hq, n);
+          const int hi_head = KV ? hq : h / p.group;  // head of the inner tensors (Q, dO or K, V)
           if (!mbar_wait(bar(L::kInEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
             ok = false;
             break;
@@ -173,8 +201,8 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t dst = sbase + L::kInner + ring.stage * 2 * kTileBytes;
           const int row = n * kBlockM;
           for (int c = 0; c < 2; ++c) {
-            tma_load_4d(dst + c * kBoxBytes, &tm_i0, fb, c * 64, h, row, b, pol);
-            tma_load_4d(dst + kTileBytes + c * kBoxBytes, &tm_i1, fb, c * 64, h, row, b, pol);
+            tma_load_4d(dst + c * kBoxBytes, &tm_i0, fb, c * 64, hi_head, row, b, pol);
+            tma_load_4d(dst + kTileBytes + c * kBoxBytes, &tm_i1, fb, c * 64, hi_head, row, b, pol);
           }
           ring.advance<2>();
         }
@@ -230,7 +258,8 @@ __global__ void __launch_bounds__(192, 1)
         outer_full_par ^= 1u;
         if (!mbar_wait(bar(L::kAccEmpty), acc_empty_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
         acc_empty_par ^= 1u;
-        for (int n = lo; n < hi && ok; ++n) {
+        const int steps = bwd_steps<KV>(p, lo, hi);
+        for (int st = 0; st < steps && ok; ++st) {
           if (!mbar_wait(bar(L::kInFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
           tc_fence_after();
           const int in0 = L::kInner + ring.stage * 2 * kTileBytes, in1 = in0 + kTileBytes;
@@ -243,10 +272,10 @@ __global__ void __launch_bounds__(192, 1)
             if (!mbar_wait(bar(L::kPFull + ch), p_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
             tc_fence_after();
             if (KV) {
-              mma_ts(256, 0, in1, n > lo, ch);    // dV += P^T dO_i
-              mma_ts(384, 128, in0, n > lo, ch);  // dK += dS^T Q_i
+              mma_ts(256, 0, in1, st > 0, ch);    // dV += P^T dO_i
+              mma_ts(384, 128, in0, st > 0, ch);  // dK += dS^T Q_i
             } else {
-              mma_ts(256, 128, in0, n > lo, ch);  // dQ += dS K_j
+              mma_ts(256, 128, in0, st > 0, ch);  // dQ += dS K_j
             }
           }
           if (!ok) break;
@@ -278,7 +307,8 @@ __global__ void __launch_bounds__(192, 1)
       const int o0 = idx * kBlockM;
       bwd_range<KV, Causal>(p, o0, lo, hi);
       const int mine = o0 + row;  // this thread's key (KV) or query row (Q)
-      const int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.stat_stride;  // LSE / D row base
+      // LSE / D row base (Q mode: this work tile's head; KV mode: set per step below)
+      int64_t stat0 = (static_cast<int64_t>(b) * p.heads + h) * p.stat_stride;
       // Q mode: this row's statistics (rows past Sq read row Sq-1 and are not stored)
       float2 lse2_row = make_float2(0.f, 0.f), d_row = make_float2(0.f, 0.f);
       if (!KV) {
@@ -286,7 +316,11 @@ __global__ void __launch_bounds__(192, 1)
         lse2_row.x = lse2_row.y = -p.lse2[stat0 + r];
         d_row.x = d_row.y = -p.dsum[stat0 + r];
       }
-      for (int n = lo; n < hi; ++n) {
+      const int steps = bwd_steps<KV>(p, lo, hi);
+      for (int st = 0; st < steps; ++st) {
+        int hq, n;
+        bwd_step<KV>(p, h, lo, hi, st, hq, n);
+        if (KV) stat0 = (static_cast<int64_t>(b) * p.heads + hq) * p.stat_stride;
         if (!warp_wait(bar(L::kSFull), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         s_par ^= 1u;
         tc_fence_after();
@@ -359,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
       if (hi <= lo) {
         // nothing attends this tile (KV mode: keys no query row sees): zero gradients
         if (KV && mine < p.sk) {
-          const int64_t off = ((static_cast<int64_t>(b) * p.sk + mine) * p.heads + h) * kHeadDim;
+          const int64_t off = ((static_cast<int64_t>(b) * p.sk + mine) * p.kv_heads + h) * kHeadDim;
           uint4* d0 = reinterpret_cast<uint4*>(p.g0 + off);
           uint4* d1 = reinterpret_cast<uint4*>(p.g1 + off);
 #pragma unroll
@@ -374,7 +408,7 @@ __global__ void __launch_bounds__(192, 1)
       acc_full_par ^= 1u;
       tc_fence_after();
       const int limit = KV ? p.sk : p.sq;
-      const int64_t off = ((static_cast<int64_t>(b) * limit + mine) * p.heads + h) * kHeadDim;
+      const int64_t off = ((static_cast<int64_t>(b) * limit + mine) * (KV ? p.kv_heads : p.heads) + h) * kHeadDim;
 #pragma unroll 1
       for (int g = 0; g < (KV ? 2 : 1); ++g) {
         // KV: g = 0 dK (column 384, times scale), g = 1 dV (column 256); Q: dQ (column 256, times scale)

@@ -617,10 +617,10 @@ extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, 
 namespace fav4 {
 namespace {
 
-bool bwd_args_valid(const Fav4BwdArgs* a, int causal) {
+bool bwd_args_valid(const Fav4BwdArgs* a, int kv_heads, int causal) {
   if (!a || !a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
       a->batch <= 0 || a->heads <= 0 || a->sq <= 0 || a->sk <= 0 || (causal != 0 && causal != 1) ||
-      !std::isfinite(a->scale) || a->scale <= 0)
+      !std::isfinite(a->scale) || a->scale <= 0 || kv_heads <= 0 || a->heads % kv_heads != 0)
     return false;
   if (a->batch > INT_MAX / a->heads || a->heads > INT_MAX / 128 || a->sq > INT_MAX / (a->heads * 128) ||
       a->sk > INT_MAX / (a->heads * 128))
@@ -649,7 +649,7 @@ int launch_bwd(const BwdParams& base, const CUtensorMap& o0, const CUtensorMap& 
   }
   BwdParams p = base;
   p.num_outer = (outer_len + kBlockM - 1) / kBlockM;
-  const int64_t tiles = static_cast<int64_t>(p.batch) * p.heads * p.num_outer;
+  const int64_t tiles = static_cast<int64_t>(p.batch) * (KV ? p.kv_heads : p.heads) * p.num_outer;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
   p.num_tiles = static_cast<int>(tiles);
   const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
@@ -675,7 +675,7 @@ int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CU
   }
   BwdFusedParams p = base;
   p.num_outer = (p.sk + kBlockN - 1) / kBlockN;
-  const int64_t tiles = static_cast<int64_t>(p.batch) * p.heads * p.num_outer;
+  const int64_t tiles = static_cast<int64_t>(p.batch) * p.kv_heads * p.num_outer;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
   p.num_tiles = static_cast<int>(tiles);
   const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
@@ -704,16 +704,16 @@ struct BwdSetup {
 };
 
 // Validation, tensor maps and the preprocess (D, LSE * log2(e)) shared by both paths.
-int bwd_prepare(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                BwdSetup* st) {
-  if (!bwd_args_valid(a, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+int bwd_prepare(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspace, size_t workspace_bytes,
+                cudaStream_t stream, BwdSetup* st) {
+  if (!bwd_args_valid(a, kv_heads, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
       workspace_bytes < fav4_bshd_backward_workspace_bytes(a))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaGetDevice(&st->dev);
   if (e != cudaSuccess) return e;
   if (!device_info(st->dev, &st->info)) return cudaErrorInvalidDevice;
-  if (!encode_bshd(&st->tq, a->q, a->batch, a->sq, a->heads) || !encode_bshd(&st->tk, a->k, a->batch, a->sk, a->heads) ||
-      !encode_bshd(&st->tv, a->v, a->batch, a->sk, a->heads) ||
+  if (!encode_bshd(&st->tq, a->q, a->batch, a->sq, a->heads) || !encode_bshd(&st->tk, a->k, a->batch, a->sk, kv_heads) ||
+      !encode_bshd(&st->tv, a->v, a->batch, a->sk, kv_heads) ||
       !encode_bshd(&st->tdo, a->dout, a->batch, a->sq, a->heads))
     return cudaErrorInvalidValue;
   st->stat_stride = (a->sq + kBlockM - 1) / kBlockM * kBlockM;
@@ -738,10 +738,14 @@ extern "C" size_t fav4_bshd_backward_workspace_bytes(const Fav4BwdArgs* a) {
   return 2 * fav4::bwd_stat_bytes(a) + fav4::bwd_acc_bytes(a);
 }
 
-extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes,
-                                  cudaStream_t stream) {
+namespace fav4 {
+namespace {
+
+int backward_fused(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream) {
   fav4::BwdSetup st;
-  cudaError_t e = static_cast<cudaError_t>(fav4::bwd_prepare(a, causal, workspace, workspace_bytes, stream, &st));
+  cudaError_t e =
+      static_cast<cudaError_t>(fav4::bwd_prepare(a, kv_heads, causal, workspace, workspace_bytes, stream, &st));
   if (e != cudaSuccess) return e;
   float* acc = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 2 * fav4::bwd_stat_bytes(a));
   const int nq = st.stat_stride / fav4::kBlockM;
@@ -758,6 +762,8 @@ extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* worksp
   p.heads = a->heads;
   p.sq = a->sq;
   p.sk = a->sk;
+  p.kv_heads = kv_heads;
+  p.group = a->heads / kv_heads;
   p.stat_stride = st.stat_stride;
   p.scale = a->scale;
   p.scale_log2 = a->scale * 1.4426950408889634f;
@@ -774,10 +780,11 @@ extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* worksp
   return cudaGetLastError();
 }
 
-extern "C" int fav4_bshd_backward_deterministic(const Fav4BwdArgs* a, int causal, void* workspace,
-                                                size_t workspace_bytes, cudaStream_t stream) {
+int backward_deterministic(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream) {
   fav4::BwdSetup st;
-  cudaError_t e = static_cast<cudaError_t>(fav4::bwd_prepare(a, causal, workspace, workspace_bytes, stream, &st));
+  cudaError_t e =
+      static_cast<cudaError_t>(fav4::bwd_prepare(a, kv_heads, causal, workspace, workspace_bytes, stream, &st));
   if (e != cudaSuccess) return e;
   const fav4::DeviceInfo& info = st.info;
   const int dev = st.dev;
@@ -792,6 +799,8 @@ extern "C" int fav4_bshd_backward_deterministic(const Fav4BwdArgs* a, int causal
   p.heads = a->heads;
   p.sq = a->sq;
   p.sk = a->sk;
+  p.kv_heads = kv_heads;
+  p.group = a->heads / kv_heads;
   p.scale = a->scale;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.status = info.status;
@@ -809,6 +818,28 @@ extern "C" int fav4_bshd_backward_deterministic(const Fav4BwdArgs* a, int causal
   pq.g1 = nullptr;
   return causal ? fav4::launch_bwd<false, true>(pq, tq, tdo, tk, tv, a->sq, info, dev, stream)
                 : fav4::launch_bwd<false, false>(pq, tq, tdo, tk, tv, a->sq, info, dev, stream);
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_backward(const Fav4BwdArgs* a, int causal, void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream) {
+  if (!a) return cudaErrorInvalidValue;
+  return fav4::backward_fused(a, a->heads, causal, workspace, workspace_bytes, stream);
+}
+
+extern "C" int fav4_bshd_backward_deterministic(const Fav4BwdArgs* a, int causal, void* workspace,
+                                                size_t workspace_bytes, cudaStream_t stream) {
+  if (!a) return cudaErrorInvalidValue;
+  return fav4::backward_deterministic(a, a->heads, causal, workspace, workspace_bytes, stream);
+}
+
+extern "C" int fav4_bshd_backward_gqa(const Fav4BwdArgs* a, int kv_heads, int causal, int deterministic,
+                                      void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!a || (deterministic != 0 && deterministic != 1)) return cudaErrorInvalidValue;
+  return deterministic ? fav4::backward_deterministic(a, kv_heads, causal, workspace, workspace_bytes, stream)
+                       : fav4::backward_fused(a, kv_heads, causal, workspace, workspace_bytes, stream);
 }
 
 extern "C" int fav4_bshd_pipeline_status(int clear) {

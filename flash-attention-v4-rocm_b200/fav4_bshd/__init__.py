@@ -87,6 +87,9 @@ def _bind(lib):
     lib.fav4_bshd_backward.restype = C.c_int
     lib.fav4_bshd_backward_deterministic.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.fav4_bshd_backward_deterministic.restype = C.c_int
+    lib.fav4_bshd_backward_gqa.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                           C.c_void_p]
+    lib.fav4_bshd_backward_gqa.restype = C.c_int
     lib.fav4_bshd_forward_varlen.argtypes = [C.POINTER(VarlenArgs), C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_varlen.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
@@ -298,13 +301,16 @@ class Runner:
 
     def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None, deterministic=False):
         """dQ, dK, dV through fav4_bshd_backward, or fav4_bshd_backward_deterministic
-        (all BF16 BSHD CUDA tensors, lse the forward's FP32 [B, H, Sq]). The
-        workspace is allocated with torch and kept for the next call."""
+        (all BF16 BSHD CUDA tensors, lse the forward's FP32 [B, H, Sq]). k, v, dk,
+        dv may have fewer heads than q, a divisor of q's (grouped-query attention,
+        through fav4_bshd_backward_gqa). The workspace is allocated with torch and
+        kept for the next call."""
         import torch
         for x in (q, k, v, o, dout, dq, dk, dv):
             assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
         b, sq, h, d = q.shape
-        assert d == HEAD_DIM and k.shape == v.shape == dk.shape == dv.shape and k.shape[0] == b and k.shape[2] == h
+        hk = k.shape[2]
+        assert d == HEAD_DIM and k.shape == v.shape == dk.shape == dv.shape and k.shape[0] == b and h % hk == 0
         assert o.shape == dout.shape == dq.shape == q.shape
         assert lse.shape == (b, h, sq) and lse.dtype == torch.float32 and lse.is_contiguous()
         scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
@@ -313,8 +319,12 @@ class Runner:
         ws = getattr(self, "_bwd_ws", None)
         if ws is None or ws.numel() < need or ws.device != q.device:
             ws = self._bwd_ws = torch.empty(need, dtype=torch.uint8, device=q.device)
-        fn = self.lib.fav4_bshd_backward_deterministic if deterministic else self.lib.fav4_bshd_backward
-        status = fn(C.byref(a), int(causal), ws.data_ptr(), ws.numel(), _stream(stream))
+        if hk != h:
+            status = self.lib.fav4_bshd_backward_gqa(C.byref(a), hk, int(causal), int(bool(deterministic)),
+                                                     ws.data_ptr(), ws.numel(), _stream(stream))
+        else:
+            fn = self.lib.fav4_bshd_backward_deterministic if deterministic else self.lib.fav4_bshd_backward
+            status = fn(C.byref(a), int(causal), ws.data_ptr(), ws.numel(), _stream(stream))
         if status:
             raise RuntimeError(f"backward: CUDA status {status}")
 

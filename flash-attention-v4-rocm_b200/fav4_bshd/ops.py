@@ -20,9 +20,10 @@ The CUDA kernel runs through ``fav4_bshd_forward`` on the current stream, so
 the operator can be captured in a CUDA graph. A fake (meta) implementation
 gives shapes to FakeTensor tracing and ``torch.compile`` graphs, so the op
 composes with both. Gradients of O with respect to q, k, v come from
-``fav4_bshd_backward``; they need the LSE, so call the op with
-``return_lse=True`` (``attention()`` does). A gradient through the LSE output
-and grouped-query gradients are not implemented and raise.
+``fav4_bshd_backward`` (``fav4_bshd_backward_gqa`` for grouped-query
+attention: dK and dV of a K/V head sum over its query heads); they need the
+LSE, so call the op with ``return_lse=True`` (``attention()`` does). A gradient
+through the LSE output is not implemented and raises.
 """
 from __future__ import annotations
 
@@ -93,8 +94,6 @@ def _backward(ctx, grad_o, grad_lse):
         raise NotImplementedError("fav4::bshd_forward: the gradient through the LSE output is not implemented")
     if not ctx.has_lse:
         raise RuntimeError("fav4::bshd_forward: gradients need return_lse=True (fav4_bshd.ops.attention does this)")
-    if k.shape[2] != q.shape[2]:
-        raise NotImplementedError("fav4::bshd_forward: grouped-query gradients are not implemented")
     if grad_o is None:
         return None, None, None, None, None, None, None
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)

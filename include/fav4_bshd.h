@@ -196,6 +196,16 @@ int fav4_bshd_backward(const Fav4BwdArgs* args, int causal, void* workspace, siz
 int fav4_bshd_backward_deterministic(const Fav4BwdArgs* args, int causal, void* workspace,
                                      size_t workspace_bytes, cudaStream_t stream);
 
+/* Grouped-query backward: k, v, dk and dv are [batch, sk, kv_heads, 128]
+ * (kv_heads divides args->heads; query head h uses K/V head
+ * h / (heads / kv_heads), as in fav4_bshd_forward_gqa). dK and dV of a K/V
+ * head sum over the query heads of its group. deterministic = 0 takes the
+ * fused path of fav4_bshd_backward, 1 the path of
+ * fav4_bshd_backward_deterministic. Same workspace; kv_heads == heads is
+ * fav4_bshd_backward / fav4_bshd_backward_deterministic. */
+int fav4_bshd_backward_gqa(const Fav4BwdArgs* args, int kv_heads, int causal, int deterministic,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* One output of fav4_bshd_forward_host: host buffers for O (BF16
  * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and
  * the mask and config it is computed with. */

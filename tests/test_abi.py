@@ -237,6 +237,12 @@ def test_backward_rejects_invalid_arguments(lib):
         assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
         assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
         assert f(C.byref(good), 0, None, need, None) == INVALID
+    g = lib.fav4_bshd_backward_gqa
+    for kv, det in ((0, 0), (3, 0), (-2, 1), (8, 0), (2, 2), (2, -1)):
+        assert g(C.byref(good), kv, 0, det, ws, need, None) == INVALID, (kv, det)
+    assert g(C.byref(bwd(q=None)), 2, 0, 0, ws, need, None) == INVALID
+    assert g(None, 2, 0, 0, ws, need, None) == INVALID
+    assert g(C.byref(good), 2, 2, 0, ws, need, None) == INVALID     # bad mode
 
 
 def test_varlen_rejects_invalid_arguments(lib):

@@ -87,6 +87,25 @@ def test_gradients_through_the_operator(runner):
     assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
 
 
+def test_gqa_gradients_through_the_operator(runner):
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    q = torch.randn((2, 300, 8, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    k, v = (torch.randn((2, 400, 2, 128), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    do = torch.randn_like(q)
+    qg, kg, vg = (x.clone().requires_grad_(True) for x in (q, k, v))
+    o = ops.attention(qg, kg, vg, causal=True)
+    o.backward(do)
+    lse = torch.empty((2, 8, 300), device="cuda")
+    o2 = torch.empty_like(q)
+    runner.call_gqa(q, k, v, o2, lse, True, 0, 1 / math.sqrt(128))
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    runner.backward(q, k, v, o2, do, lse, dq, dk, dv, True, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert torch.equal(o.detach(), o2)
+    assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
+    assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
+
+
 def test_gradient_limits_raise():
     q, k, v = _inputs(1, 2, 128, 128, seed=10)
     qg = q.clone().requires_grad_(True)
