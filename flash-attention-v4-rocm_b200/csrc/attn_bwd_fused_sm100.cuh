@@ -51,7 +51,13 @@ struct BwdFusedParams {
   __nv_bfloat16* dv;
   int batch, heads, sq, sk;
   int kv_heads, group;  // K/V heads, heads / kv_heads
-  int stat_stride;    // q tiles * 128
+  // Packed sequences (Varlen): batch entry b is rows [cu_q[b], cu_q[b+1]) of Q, O, dO, dQ against
+  // [cu_k[b], cu_k[b+1]) of K, V, dK, dV; sq / sk are then the packed totals and max_sq / max_sk
+  // bound every sequence (longer ones are cut to them).
+  const int* cu_q;
+  const int* cu_k;
+  int max_sq, max_sk;
+  int stat_stride;    // q tiles * 128 (q tiles of max_sq for packed sequences)
   float scale, scale_log2;
   int num_outer;      // key tiles per (batch, head)
   int num_tiles;      // batch * kv_heads * num_outer
@@ -99,7 +105,21 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-template <bool Causal>
+// One batch entry: its first query row and key in the (packed) tensors and its lengths.
+struct BwdSeq {
+  int q0, sq, k0, sk;
+};
+template <bool Varlen>
+__device__ __forceinline__ BwdSeq bwd_seq(const BwdFusedParams& p, int b) {
+  if (!Varlen) return BwdSeq{0, p.sq, 0, p.sk};
+  // offsets clamped to the tensors and lengths to max_sq / max_sk: malformed offsets cannot move
+  // an access outside the tensors, the statistics or the accumulator
+  const int qa = min(max(__ldg(p.cu_q + b), 0), p.sq), qe = min(max(__ldg(p.cu_q + b + 1), qa), p.sq);
+  const int ka = min(max(__ldg(p.cu_k + b), 0), p.sk), ke = min(max(__ldg(p.cu_k + b + 1), ka), p.sk);
+  return BwdSeq{qa, min(qe - qa, p.max_sq), ka, min(ke - ka, p.max_sk)};
+}
+
+template <bool Causal, bool Varlen>
 __global__ void __launch_bounds__(512, 1)
     attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -160,7 +180,7 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int nq = (p.sq + kBlockM - 1) / kBlockM;
+  const int nq = p.stat_stride / kBlockM;  // query tiles per (batch entry, head) in the accumulator
 
   if (warp >= 12) {
     regs_release<kBwdOtherRegs>();
@@ -175,21 +195,26 @@ __global__ void __launch_bounds__(512, 1)
         int b, h, idx, lo, hi;
         bwd_tile<Causal>(rp, t, b, h, idx, true);
         const int o0 = idx * kBlockN;
-        bwd_range<true, Causal>(rp, o0, lo, hi);
+        const BwdSeq sq = bwd_seq<Varlen>(p, b);
+        BwdParams rt = rp;
+        rt.sq = sq.sq;
+        rt.sk = sq.sk;
+        bwd_range<true, Causal>(rt, o0, lo, hi);
         if (hi <= lo) continue;
+        const int tb = Varlen ? 0 : b;  // batch coordinate of the tensor maps
         if (!mbar_wait(bar(L::kKVEmpty), kv_empty_par, ctl, kStatusTimeoutLoad)) { ok = false; break; }
         kv_empty_par ^= 1u;
         mbar_arrive_expect_tx(bar(L::kKVFull), 2 * kTileBytes);
         armed |= 4u;
         armed_par = (armed_par & ~4u) | (kv_empty_par << 2);
         for (int c = 0; c < 2; ++c) {
-          tma_load_4d(sbase + L::kK + c * kBoxBytes, &tm_k, bar(L::kKVFull), c * 64, h, o0, b, pol);
-          tma_load_4d(sbase + L::kV + c * kBoxBytes, &tm_v, bar(L::kKVFull), c * 64, h, o0, b, pol);
+          tma_load_4d(sbase + L::kK + c * kBoxBytes, &tm_k, bar(L::kKVFull), c * 64, h, sq.k0 + o0, tb, pol);
+          tma_load_4d(sbase + L::kV + c * kBoxBytes, &tm_v, bar(L::kKVFull), c * 64, h, sq.k0 + o0, tb, pol);
         }
-        const int steps = bwd_steps<true>(rp, lo, hi);
+        const int steps = bwd_steps<true>(rt, lo, hi);
         for (int st = 0; st < steps && ok; ++st) {
           int hq, i;
-          bwd_step<true>(rp, h, lo, hi, st, hq, i);
+          bwd_step<true>(rt, h, lo, hi, st, hq, i);
           const int64_t stat_bh = (static_cast<int64_t>(b) * p.heads + hq) * p.stat_stride;
           if (!mbar_wait(bar(L::kInEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
             ok = false;
@@ -201,9 +226,10 @@ __global__ void __launch_bounds__(512, 1)
           armed_par = (armed_par & ~(1u << ring.stage)) | (ring.phase << ring.stage);
           const int row = i * kBlockM;
           for (int c = 0; c < 2; ++c) {
-            tma_load_4d(sbase + L::kQ + ring.stage * kTileBytes + c * kBoxBytes, &tm_q, fb, c * 64, hq, row, b, pol);
-            tma_load_4d(sbase + L::kDO + ring.stage * kTileBytes + c * kBoxBytes, &tm_do, fb, c * 64, hq, row, b,
-                        pol);
+            tma_load_4d(sbase + L::kQ + ring.stage * kTileBytes + c * kBoxBytes, &tm_q, fb, c * 64, hq, sq.q0 + row,
+                        tb, pol);
+            tma_load_4d(sbase + L::kDO + ring.stage * kTileBytes + c * kBoxBytes, &tm_do, fb, c * 64, hq,
+                        sq.q0 + row, tb, pol);
           }
           const uint32_t sa = sbase + L::kStat + ring.stage * L::kStatBytes;
           bulk_load(sa, p.lse2 + stat_bh + row, kBlockM * 4, fb);
@@ -268,7 +294,11 @@ __global__ void __launch_bounds__(512, 1)
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int b, h, idx, lo, hi;
         bwd_tile<Causal>(rp, t, b, h, idx, true);
-        bwd_range<true, Causal>(rp, idx * kBlockN, lo, hi);
+        const BwdSeq sq = bwd_seq<Varlen>(p, b);
+        BwdParams rt = rp;
+        rt.sq = sq.sq;
+        rt.sk = sq.sk;
+        bwd_range<true, Causal>(rt, idx * kBlockN, lo, hi);
         if (hi <= lo) continue;
         if (!mbar_wait(bar(L::kKVFull), kv_full_par, ctl, kStatusTimeoutMma)) { ok = false; break; }
         kv_full_par ^= 1u;
@@ -281,7 +311,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         mma_ss(128, L::kV, L::kDO + ring.stage * kTileBytes);  // dP^T(lo)
         tc_commit(bar(L::kDPFull));
-        const int steps = bwd_steps<true>(rp, lo, hi);
+        const int steps = bwd_steps<true>(rt, lo, hi);
         for (int st = 0; st < steps && ok; ++st) {
           const int cur = ring.stage;
           Ring nxt = ring;
@@ -340,12 +370,18 @@ __global__ void __launch_bounds__(512, 1)
       int b, h, idx, lo, hi;
       bwd_tile<Causal>(rp, t, b, h, idx, true);
       const int o0 = idx * kBlockN;
-      bwd_range<true, Causal>(rp, o0, lo, hi);
+      const BwdSeq sq = bwd_seq<Varlen>(p, b);
+      BwdParams rt = rp;
+      rt.sq = sq.sq;
+      rt.sk = sq.sk;
+      bwd_range<true, Causal>(rt, o0, lo, hi);
       const int key = o0 + row;
-      const int steps = bwd_steps<true>(rp, lo, hi);
+      // this key's row of dK / dV: [B, Sk, H_kv, 128] or packed [total_k, H_kv, 128]
+      const int64_t krow = Varlen ? static_cast<int64_t>(sq.k0) + key : static_cast<int64_t>(b) * p.sk + key;
+      const int steps = bwd_steps<true>(rt, lo, hi);
       for (int st = 0; st < steps; ++st) {
         int hq, i;
-        bwd_step<true>(rp, h, lo, hi, st, hq, i);
+        bwd_step<true>(rt, h, lo, hi, st, hq, i);
         if (!warp_wait(bar(L::kDQFull), dq_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         dq_par ^= 1u;
         tc_fence_after();
@@ -369,8 +405,8 @@ __global__ void __launch_bounds__(512, 1)
       if (!ok) break;
       if (hi <= lo) {
         // no query row sees these keys (causal, Sk > Sq): zero gradients
-        if (key < p.sk) {
-          const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.kv_heads + h) * kHeadDim;
+        if (key < sq.sk) {
+          const int64_t off = (krow * p.kv_heads + h) * kHeadDim;
           uint4* d0 = reinterpret_cast<uint4*>(p.dk + off);
           uint4* d1 = reinterpret_cast<uint4*>(p.dv + off);
 #pragma unroll
@@ -384,7 +420,7 @@ __global__ void __launch_bounds__(512, 1)
       if (!warp_wait(bar(L::kAccFull), acc_full_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
       acc_full_par ^= 1u;
       tc_fence_after();
-      const int64_t off = ((static_cast<int64_t>(b) * p.sk + key) * p.kv_heads + h) * kHeadDim;
+      const int64_t off = (krow * p.kv_heads + h) * kHeadDim;
 #pragma unroll 1
       for (int g = 0; g < 2; ++g) {
         // g = 0: dK (T3, times scale); g = 1: dV (T2)
@@ -396,7 +432,7 @@ __global__ void __launch_bounds__(512, 1)
           uint32_t a[32];
           tmem_ld32(tmem + lane_off + col + ch * 32, a);
           tmem_ld_wait();
-          if (key < p.sk) {
+          if (key < sq.sk) {
             uint4* dst = reinterpret_cast<uint4*>(dst_row + ch * 32);
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
@@ -433,12 +469,16 @@ __global__ void __launch_bounds__(512, 1)
       int b, h, idx, lo, hi;
       bwd_tile<Causal>(rp, t, b, h, idx, true);
       const int o0 = idx * kBlockN;
-      bwd_range<true, Causal>(rp, o0, lo, hi);
+      const BwdSeq sq = bwd_seq<Varlen>(p, b);
+      BwdParams rt = rp;
+      rt.sq = sq.sq;
+      rt.sk = sq.sk;
+      bwd_range<true, Causal>(rt, o0, lo, hi);
       const int key = o0 + key_lane;
-      const int steps = bwd_steps<true>(rp, lo, hi);
+      const int steps = bwd_steps<true>(rt, lo, hi);
       for (int st = 0; st < steps; ++st) {
         int hq, i;
-        bwd_step<true>(rp, h, lo, hi, st, hq, i);
+        bwd_step<true>(rt, h, lo, hi, st, hq, i);
         const float* stat = reinterpret_cast<const float*>(smem + L::kStat + ring.stage * L::kStatBytes);
         if (!warp_wait(bar(L::kInFull + ring.stage), ring.phase, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
         if (!warp_wait(bar(L::kSFull), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
@@ -446,8 +486,9 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const int q0 = i * kBlockM + half * 64;  // first query column of this half
         // masks only on boundary tiles: the causal diagonal and tails past Sq / Sk
-        const bool masked = (Causal && o0 + kBlockN - 1 > i * kBlockM) || i * kBlockM + kBlockM > p.sq ||
-                            o0 + kBlockN > p.sk;
+        // (packed sequences: rows and keys past the sequence's end belong to the next one)
+        const bool masked = (Causal && o0 + kBlockN - 1 > i * kBlockM) || i * kBlockM + kBlockM > sq.sq ||
+                            o0 + kBlockN > sq.sk;
         // ---- phase A: P^T = exp2(S^T scale log2e - LSE2) ----
         float pr[64];
 #pragma unroll
@@ -466,8 +507,8 @@ __global__ void __launch_bounds__(512, 1)
               float2 v2 = make_float2(ex2_mufu(x.x), ex2_mufu(x.y));
               if (masked) {
                 const int qa = q0 + c * 32 + e + u;
-                if (!(qa < p.sq && key < p.sk && (!Causal || key <= qa))) v2.x = 0.f;
-                if (!(qa + 1 < p.sq && key < p.sk && (!Causal || key <= qa + 1))) v2.y = 0.f;
+                if (!(qa < sq.sq && key < sq.sk && (!Causal || key <= qa))) v2.x = 0.f;
+                if (!(qa + 1 < sq.sq && key < sq.sk && (!Causal || key <= qa + 1))) v2.y = 0.f;
               }
               pr[c * 32 + e + u] = v2.x;
               pr[c * 32 + e + u + 1] = v2.y;
@@ -529,13 +570,14 @@ __global__ void __launch_bounds__(512, 1)
   }
 }
 
-// dQ = scale * accumulator, BF16 [B, Sq, H, 128]. One thread per (tile row, 32 columns):
-// eight 16-byte accumulator loads (a warp reads 512 contiguous bytes per load) and
-// four 16-byte stores of its row's 64 bytes.
+// dQ = scale * accumulator, BF16 [B, Sq, H, 128] (packed [total_q, H, 128] when cu_q is
+// given: batch entry b's rows go to cu_q[b] + r, at most max_sq of them). nq query tiles per
+// (batch entry, head) in the accumulator. One thread per (tile row, 32 columns): eight 16-byte
+// accumulator loads (a warp reads 512 contiguous bytes per load) and four 16-byte stores.
 __global__ void __launch_bounds__(256) attn_bwd_dq_convert_kernel(const float* __restrict__ acc,
                                                                   __nv_bfloat16* __restrict__ dq, int batch,
-                                                                  int heads, int sq, float scale) {
-  const int nq = (sq + kBlockM - 1) / kBlockM;
+                                                                  int heads, int sq, int nq, float scale,
+                                                                  const int* __restrict__ cu_q, int max_sq) {
   const int64_t total = static_cast<int64_t>(batch) * heads * nq * kBlockM * 4;
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -548,14 +590,62 @@ __global__ void __launch_bounds__(256) attn_bwd_dq_convert_kernel(const float* _
     const int h = static_cast<int>(bh % heads);
     const int64_t b = bh / heads;
     const int q = i * kBlockM + r;
-    if (q >= sq) continue;
+    int64_t orow;  // row of dQ
+    if (cu_q) {
+      const int qa = min(max(__ldg(cu_q + b), 0), sq), qe = min(max(__ldg(cu_q + b + 1), qa), sq);
+      if (q >= min(qe - qa, max_sq)) continue;
+      orow = qa + q;
+    } else {
+      if (q >= sq) continue;
+      orow = b * sq + q;
+    }
     const float4* src = reinterpret_cast<const float4*>(acc + tile * (kBlockM * kHeadDim)) + oct * 8 * kBlockM + r;
-    uint4* dst = reinterpret_cast<uint4*>(dq + ((b * sq + q) * heads + h) * kHeadDim + oct * 32);
+    uint4* dst = reinterpret_cast<uint4*>(dq + (orow * heads + h) * kHeadDim + oct * 32);
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float4 x = src[(2 * w) * kBlockM], y = src[(2 * w + 1) * kBlockM];
       dst[w] = make_uint4(pack_bf16x2(x.x * scale, x.y * scale), pack_bf16x2(x.z * scale, x.w * scale),
                           pack_bf16x2(y.x * scale, y.y * scale), pack_bf16x2(y.z * scale, y.w * scale));
+    }
+  }
+}
+
+// Packed sequences: D = rowsum(dO * O) and LSE * log2(e) into [B, H, stat_stride] (batch entry b's
+// row r from packed row cu_q[b] + r; 0 past the entry's length, at most max_sq), from O, dO
+// [total_q, H, 128] and the forward's LSE [H, total_q]. One warp per (b, r, h).
+__global__ void __launch_bounds__(256) attn_bwd_dsum_varlen_kernel(
+    const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
+    float* __restrict__ dsum, float* __restrict__ lse2, const int* __restrict__ cu_q, int batch, int heads,
+    int total_q, int max_sq, int stat_stride) {
+  const int64_t slots = static_cast<int64_t>(batch) * stat_stride * heads;
+  const int lane = threadIdx.x % 32;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < slots;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const int h = static_cast<int>(w % heads);
+    const int64_t br = w / heads;
+    const int r = static_cast<int>(br % stat_stride);
+    const int b = static_cast<int>(br / stat_stride);
+    const int qa = min(max(__ldg(cu_q + b), 0), total_q), qe = min(max(__ldg(cu_q + b + 1), qa), total_q);
+    const bool live = r < min(qe - qa, max_sq);
+    float s = 0.f;
+    if (live) {
+      const int64_t row = (static_cast<int64_t>(qa) + r) * heads + h;
+      const uint2 a = reinterpret_cast<const uint2*>(o + row * kHeadDim)[lane];
+      const uint2 g = reinterpret_cast<const uint2*>(dout + row * kHeadDim)[lane];
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
+        s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    }
+    if (lane == 0) {
+      const int64_t at = (static_cast<int64_t>(b) * heads + h) * stat_stride + r;
+      dsum[at] = s;
+      lse2[at] = live ? lse[static_cast<int64_t>(h) * total_q + qa + r] * 1.4426950408889634f : 0.f;
     }
   }
 }

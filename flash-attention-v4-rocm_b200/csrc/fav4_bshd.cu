@@ -657,11 +657,11 @@ int launch_bwd(const BwdParams& base, const CUtensorMap& o0, const CUtensorMap& 
   return cudaGetLastError();
 }
 
-template <bool Causal>
+template <bool Causal, bool Varlen>
 int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& tq, const CUtensorMap& tdo, const DeviceInfo& info, int dev,
                      cudaStream_t stream) {
-  auto kernel = attn_bwd_fused_kernel<Causal>;
+  auto kernel = attn_bwd_fused_kernel<Causal, Varlen>;
   constexpr int smem = BwdFusedSmem::kBytes;
   {
     static std::mutex mu;
@@ -674,7 +674,7 @@ int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CU
     }
   }
   BwdFusedParams p = base;
-  p.num_outer = (p.sk + kBlockN - 1) / kBlockN;
+  p.num_outer = ((Varlen ? p.max_sk : p.sk) + kBlockN - 1) / kBlockN;
   const int64_t tiles = static_cast<int64_t>(p.batch) * p.kv_heads * p.num_outer;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
   p.num_tiles = static_cast<int>(tiles);
@@ -692,6 +692,16 @@ size_t bwd_stat_bytes(const Fav4BwdArgs* a) {
 size_t bwd_acc_bytes(const Fav4BwdArgs* a) {
   const size_t nq = (static_cast<size_t>(a->sq) + kBlockM - 1) / kBlockM;
   return round256(static_cast<size_t>(a->batch) * a->heads * nq * kBlockM * kHeadDim * 4);
+}
+
+int launch_dq_convert(const float* acc, void* dq, int batch, int heads, int sq, int nq, float scale, const int* cu_q,
+                      int max_sq, const DeviceInfo& info, cudaStream_t stream) {
+  const int64_t threads = static_cast<int64_t>(batch) * heads * nq * kBlockM * 4;
+  const int64_t want = (threads + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(info.sms) * 16;
+  attn_bwd_dq_convert_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
+      acc, static_cast<__nv_bfloat16*>(dq), batch, heads, sq, nq, scale, cu_q, max_sq);
+  return cudaGetLastError();
 }
 
 struct BwdSetup {
@@ -769,15 +779,11 @@ int backward_fused(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspa
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.status = st.info.status;
   p.wait_limit_ns = fav4::wait_limit_ns();
-  e = static_cast<cudaError_t>(causal ? fav4::launch_bwd_fused<true>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream)
-                                      : fav4::launch_bwd_fused<false>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream));
+  e = static_cast<cudaError_t>(
+      causal ? fav4::launch_bwd_fused<true, false>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream)
+             : fav4::launch_bwd_fused<false, false>(p, st.tk, st.tv, st.tq, st.tdo, st.info, st.dev, stream));
   if (e != cudaSuccess) return e;
-  const int64_t threads = static_cast<int64_t>(a->batch) * a->heads * nq * fav4::kBlockM * 4;
-  const int64_t want = (threads + 255) / 256;
-  const int64_t cap = static_cast<int64_t>(st.info.sms) * 16;
-  fav4::attn_bwd_dq_convert_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
-      acc, static_cast<__nv_bfloat16*>(a->dq), a->batch, a->heads, a->sq, a->scale);
-  return cudaGetLastError();
+  return launch_dq_convert(acc, a->dq, a->batch, a->heads, a->sq, nq, a->scale, nullptr, 0, st.info, stream);
 }
 
 int backward_deterministic(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspace,
@@ -840,6 +846,106 @@ extern "C" int fav4_bshd_backward_gqa(const Fav4BwdArgs* a, int kv_heads, int ca
   if (!a || (deterministic != 0 && deterministic != 1)) return cudaErrorInvalidValue;
   return deterministic ? fav4::backward_deterministic(a, kv_heads, causal, workspace, workspace_bytes, stream)
                        : fav4::backward_fused(a, kv_heads, causal, workspace, workspace_bytes, stream);
+}
+
+namespace fav4 {
+namespace {
+
+bool varlen_bwd_valid(const Fav4VarlenBwdArgs* a, int causal) {
+  if (!a || !a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
+      !a->cu_seqlens_q || !a->cu_seqlens_k || a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 ||
+      a->heads % a->kv_heads != 0 || a->total_q <= 0 || a->total_k <= 0 || a->max_sq <= 0 || a->max_sk <= 0 ||
+      a->max_sq > a->total_q || a->max_sk > a->total_k || (causal != 0 && causal != 1) || !std::isfinite(a->scale) ||
+      a->scale <= 0)
+    return false;
+  if (a->heads > INT_MAX / 128 || a->total_q > INT_MAX / (a->heads * 128) ||
+      a->total_k > INT_MAX / (a->kv_heads * 128) || a->batch > INT_MAX / a->heads - 1)
+    return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                       reinterpret_cast<uintptr_t>(a->v) | reinterpret_cast<uintptr_t>(a->o) |
+                       reinterpret_cast<uintptr_t>(a->dout) | reinterpret_cast<uintptr_t>(a->dq) |
+                       reinterpret_cast<uintptr_t>(a->dk) | reinterpret_cast<uintptr_t>(a->dv);
+  const uintptr_t al4 = reinterpret_cast<uintptr_t>(a->lse) | reinterpret_cast<uintptr_t>(a->cu_seqlens_q) |
+                        reinterpret_cast<uintptr_t>(a->cu_seqlens_k);
+  return (al & 15) == 0 && (al4 & 3) == 0;
+}
+
+size_t varlen_stat_bytes(const Fav4VarlenBwdArgs* a) {
+  const size_t nq = (static_cast<size_t>(a->max_sq) + kBlockM - 1) / kBlockM;
+  return round256(static_cast<size_t>(a->batch) * a->heads * nq * kBlockM * 4);
+}
+size_t varlen_acc_bytes(const Fav4VarlenBwdArgs* a) {
+  const size_t nq = (static_cast<size_t>(a->max_sq) + kBlockM - 1) / kBlockM;
+  return round256(static_cast<size_t>(a->batch) * a->heads * nq * kBlockM * kHeadDim * 4);
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" size_t fav4_bshd_backward_varlen_workspace_bytes(const Fav4VarlenBwdArgs* a) {
+  if (!fav4::varlen_bwd_valid(a, 0)) return 0;
+  return 2 * fav4::varlen_stat_bytes(a) + fav4::varlen_acc_bytes(a);
+}
+
+extern "C" int fav4_bshd_backward_varlen(const Fav4VarlenBwdArgs* a, int causal, void* workspace,
+                                         size_t workspace_bytes, cudaStream_t stream) {
+  if (!fav4::varlen_bwd_valid(a, causal) || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < fav4_bshd_backward_varlen_workspace_bytes(a))
+    return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  fav4::DeviceInfo info;
+  if (!fav4::device_info(dev, &info)) return cudaErrorInvalidDevice;
+  CUtensorMap tq, tk, tv, tdo;
+  if (!fav4::encode_bshd(&tq, a->q, 1, a->total_q, a->heads) || !fav4::encode_bshd(&tk, a->k, 1, a->total_k, a->kv_heads) ||
+      !fav4::encode_bshd(&tv, a->v, 1, a->total_k, a->kv_heads) ||
+      !fav4::encode_bshd(&tdo, a->dout, 1, a->total_q, a->heads))
+    return cudaErrorInvalidValue;
+  const int nq = (a->max_sq + fav4::kBlockM - 1) / fav4::kBlockM;
+  const int stat_stride = nq * fav4::kBlockM;
+  float* dsum = static_cast<float*>(workspace);
+  float* lse2 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + fav4::varlen_stat_bytes(a));
+  float* acc = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 2 * fav4::varlen_stat_bytes(a));
+  {
+    const int64_t slots = static_cast<int64_t>(a->batch) * stat_stride * a->heads;
+    const int64_t want = (slots + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(info.sms) * 16;
+    fav4::attn_bwd_dsum_varlen_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, dsum, lse2,
+        a->cu_seqlens_q, a->batch, a->heads, a->total_q, a->max_sq, stat_stride);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  e = cudaMemsetAsync(acc, 0, static_cast<size_t>(a->batch) * a->heads * nq * fav4::kBlockM * fav4::kHeadDim * 4,
+                      stream);
+  if (e != cudaSuccess) return e;
+  fav4::BwdFusedParams p = {};
+  p.lse2 = lse2;
+  p.dsum = dsum;
+  p.dq_acc = acc;
+  p.dk = static_cast<__nv_bfloat16*>(a->dk);
+  p.dv = static_cast<__nv_bfloat16*>(a->dv);
+  p.batch = a->batch;
+  p.heads = a->heads;
+  p.sq = a->total_q;
+  p.sk = a->total_k;
+  p.kv_heads = a->kv_heads;
+  p.group = a->heads / a->kv_heads;
+  p.cu_q = a->cu_seqlens_q;
+  p.cu_k = a->cu_seqlens_k;
+  p.max_sq = a->max_sq;
+  p.max_sk = a->max_sk;
+  p.stat_stride = stat_stride;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.status = info.status;
+  p.wait_limit_ns = fav4::wait_limit_ns();
+  e = static_cast<cudaError_t>(causal ? fav4::launch_bwd_fused<true, true>(p, tk, tv, tq, tdo, info, dev, stream)
+                                      : fav4::launch_bwd_fused<false, true>(p, tk, tv, tq, tdo, info, dev, stream));
+  if (e != cudaSuccess) return e;
+  return fav4::launch_dq_convert(acc, a->dq, a->batch, a->heads, a->total_q, nq, a->scale, a->cu_seqlens_q,
+                                 a->max_sq, info, stream);
 }
 
 extern "C" int fav4_bshd_pipeline_status(int clear) {

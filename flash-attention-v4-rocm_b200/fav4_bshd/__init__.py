@@ -42,6 +42,15 @@ class VarlenArgs(C.Structure):
         (n, C.c_int) for n in ("batch", "heads", "kv_heads", "max_sq", "total_q", "total_k")] + [("scale", C.c_float)]
 
 
+class VarlenBwdArgs(C.Structure):
+    """Fav4VarlenBwdArgs (include/fav4_bshd.h): backward of packed sequences."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "dout", "lse", "dq", "dk", "dv", "cu_seqlens_q",
+                                          "cu_seqlens_k")] + [
+        (n, C.c_int) for n in ("batch", "heads", "kv_heads", "max_sq", "max_sk", "total_q", "total_k")] + [
+        ("scale", C.c_float)]
+
+
 class HostOut(C.Structure):
     """Fav4HostOut (include/fav4_bshd.h): one output of fav4_bshd_forward_host."""
 
@@ -90,6 +99,10 @@ def _bind(lib):
     lib.fav4_bshd_backward_gqa.argtypes = [C.POINTER(BwdArgs), C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                                            C.c_void_p]
     lib.fav4_bshd_backward_gqa.restype = C.c_int
+    lib.fav4_bshd_backward_varlen_workspace_bytes.argtypes = [C.POINTER(VarlenBwdArgs)]
+    lib.fav4_bshd_backward_varlen_workspace_bytes.restype = C.c_size_t
+    lib.fav4_bshd_backward_varlen.argtypes = [C.POINTER(VarlenBwdArgs), C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.fav4_bshd_backward_varlen.restype = C.c_int
     lib.fav4_bshd_forward_varlen.argtypes = [C.POINTER(VarlenArgs), C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward_varlen.restype = C.c_int
     lib.fav4_bshd_pipeline_status.argtypes = [C.c_int]
@@ -298,6 +311,35 @@ class Runner:
         status = self.lib.fav4_bshd_forward_varlen(C.byref(a), int(causal), config, _stream(stream))
         if status:
             raise RuntimeError(f"varlen config {config}: CUDA status {status}")
+
+    def backward_varlen(self, q, k, v, o, dout, lse, dq, dk, dv, cu_q, cu_k, max_sq, max_sk, causal, scale=None,
+                        stream=None):
+        """Gradients of call_varlen (fav4_bshd_backward_varlen): q, o, dout, dq
+        [total_q, H, 128]; k, v, dk, dv [total_k, H_kv, 128]; lse the forward's FP32
+        [H, total_q]; cu_q, cu_k int32 CUDA [batch + 1]; max_sq / max_sk bound the
+        sequence lengths. The workspace is allocated with torch and kept."""
+        import torch
+        for x in (q, k, v, o, dout, dq, dk, dv):
+            assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous() and x.dim() == 3
+        assert cu_q.dtype == cu_k.dtype == torch.int32 and cu_q.is_cuda and cu_k.is_cuda
+        assert cu_q.numel() == cu_k.numel() >= 2
+        assert o.shape == dout.shape == dq.shape == q.shape and k.shape == v.shape == dk.shape == dv.shape
+        tq, h, _ = q.shape
+        tk, hk, _ = k.shape
+        assert lse.shape == (h, tq) and lse.dtype == torch.float32 and lse.is_contiguous()
+        scale = 1 / math.sqrt(HEAD_DIM) if scale is None else scale
+        a = VarlenBwdArgs(*(x.data_ptr() for x in (q, k, v, o, dout, lse, dq, dk, dv, cu_q, cu_k)),
+                          cu_q.numel() - 1, h, hk, max_sq, max_sk, tq, tk, scale)
+        need = self.lib.fav4_bshd_backward_varlen_workspace_bytes(C.byref(a))
+        if need == 0:
+            raise RuntimeError("backward_varlen: invalid arguments")
+        ws = getattr(self, "_bwd_ws", None)
+        if ws is None or ws.numel() < need or ws.device != q.device:
+            ws = self._bwd_ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+        status = self.lib.fav4_bshd_backward_varlen(C.byref(a), int(causal), ws.data_ptr(), ws.numel(),
+                                                    _stream(stream))
+        if status:
+            raise RuntimeError(f"backward_varlen: CUDA status {status}")
 
     def backward(self, q, k, v, o, dout, lse, dq, dk, dv, causal, scale=None, stream=None, deterministic=False):
         """dQ, dK, dV through fav4_bshd_backward, or fav4_bshd_backward_deterministic

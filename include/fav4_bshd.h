@@ -206,6 +206,31 @@ int fav4_bshd_backward_deterministic(const Fav4BwdArgs* args, int causal, void* 
 int fav4_bshd_backward_gqa(const Fav4BwdArgs* args, int kv_heads, int causal, int deterministic,
                            void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Backward of fav4_bshd_forward_varlen (packed sequences). q, o, dout, dq:
+ * [total_q, heads, 128]; k, v, dk, dv: [total_k, kv_heads, 128]; lse: the
+ * forward's FP32 [heads, total_q]; cu_seqlens_q / cu_seqlens_k: device int32
+ * offsets, batch + 1 of them, as in Fav4VarlenArgs. max_sq / max_sk bound
+ * every sequence's length (rows or keys past them are not computed); both
+ * size the workspace. The fused path (FP32 dQ reductions); keys no query row
+ * of their sequence sees get zero gradients. */
+struct Fav4VarlenBwdArgs {
+  const void *q, *k, *v, *o, *dout;
+  const float* lse;
+  void *dq, *dk, *dv;
+  const int *cu_seqlens_q, *cu_seqlens_k;
+  int batch, heads, kv_heads, max_sq, max_sk, total_q, total_k;
+  float scale;
+};
+typedef struct Fav4VarlenBwdArgs Fav4VarlenBwdArgs;
+
+/* Device workspace fav4_bshd_backward_varlen needs (0 on invalid arguments). */
+size_t fav4_bshd_backward_varlen_workspace_bytes(const Fav4VarlenBwdArgs* args);
+
+/* Returns 0, cudaErrorInvalidValue (1) on invalid arguments, else the first
+ * failing launch status. */
+int fav4_bshd_backward_varlen(const Fav4VarlenBwdArgs* args, int causal, void* workspace, size_t workspace_bytes,
+                              cudaStream_t stream);
+
 /* One output of fav4_bshd_forward_host: host buffers for O (BF16
  * [batch, sq, heads, 128]) and optionally LSE (FP32 [batch, heads, sq]), and
  * the mask and config it is computed with. */

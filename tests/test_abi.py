@@ -245,6 +245,33 @@ def test_backward_rejects_invalid_arguments(lib):
     assert g(C.byref(good), 2, 2, 0, ws, need, None) == INVALID     # bad mode
 
 
+def test_varlen_backward_rejects_invalid_arguments(lib):
+    def vb(**kw):
+        a = dict(q=A16, k=A16 * 2, v=A16 * 3, o=A16 * 4, dout=A16 * 5, lse=A16 * 6, dq=A16 * 7, dk=A16 * 8,
+                 dv=A16 * 9, cu_seqlens_q=A16 * 10, cu_seqlens_k=A16 * 11, batch=3, heads=8, kv_heads=2, max_sq=100,
+                 max_sk=150, total_q=200, total_k=300, scale=0.1)
+        a.update(kw)
+        return F.VarlenBwdArgs(*(a[n] for n in ("q", "k", "v", "o", "dout", "lse", "dq", "dk", "dv", "cu_seqlens_q",
+                                                "cu_seqlens_k", "batch", "heads", "kv_heads", "max_sq", "max_sk",
+                                                "total_q", "total_k", "scale")))
+    good = vb()
+    need = lib.fav4_bshd_backward_varlen_workspace_bytes(C.byref(good))
+    # D and LSE * log2(e) over one padded query tile per (sequence, head), then the FP32 accumulator
+    assert need == 2 * (3 * 8 * 128 * 4) + 3 * 8 * 128 * 128 * 4
+    ws = A16 * 256
+    f = lib.fav4_bshd_backward_varlen
+    for kw in (dict(q=None), dict(dout=None), dict(lse=None), dict(dq=None), dict(cu_seqlens_q=None),
+               dict(cu_seqlens_k=None), dict(batch=0), dict(kv_heads=3), dict(kv_heads=0), dict(max_sq=0),
+               dict(max_sq=201), dict(max_sk=0), dict(max_sk=301), dict(total_k=0), dict(scale=-1.0),
+               dict(scale=float("inf")), dict(dk=A16 * 8 + 8), dict(lse=A16 * 6 + 2), dict(cu_seqlens_k=A16 * 11 + 2)):
+        assert lib.fav4_bshd_backward_varlen_workspace_bytes(C.byref(vb(**kw))) == 0, kw
+        assert f(C.byref(vb(**kw)), 0, ws, need, None) == INVALID, kw
+    assert f(C.byref(good), 2, ws, need, None) == INVALID        # bad mode
+    assert f(C.byref(good), 0, ws, need - 1, None) == INVALID    # workspace too small
+    assert f(C.byref(good), 0, ws + 128, need, None) == INVALID  # misaligned
+    assert f(None, 0, ws, need, None) == INVALID
+
+
 def test_varlen_rejects_invalid_arguments(lib):
     def va(**kw):
         a = dict(q=A16, k=A16 * 2, v=A16 * 3, o=A16 * 4, lse=None, cu_seqlens_q=A16 * 5, cu_seqlens_k=A16 * 6,
