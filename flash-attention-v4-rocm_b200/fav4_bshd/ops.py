@@ -16,6 +16,10 @@ output allocation, the current stream and tracing:
 * Returns O (BF16, q's shape) and LSE (FP32 ``[B, H, Sq]``, natural log), or
   an empty LSE tensor when ``return_lse`` is False.
 
+``torch.ops.fav4.varlen_forward`` (``varlen_attention()``) is the same for
+packed sequences ``[total, H, 128]`` with int32 ``cu_seqlens`` offsets,
+differentiable through ``fav4_bshd_backward_varlen``.
+
 The CUDA kernel runs through ``fav4_bshd_forward`` on the current stream, so
 the operator can be captured in a CUDA graph. A fake (meta) implementation
 gives shapes to FakeTensor tracing and ``torch.compile`` graphs, so the op
@@ -104,6 +108,78 @@ def _backward(ctx, grad_o, grad_lse):
 
 
 bshd_forward.register_autograd(_backward, setup_context=_setup_context)
+
+
+def _check_varlen(q, k, v, cu_q, cu_k, max_sq, max_sk):
+    torch._check(q.dim() == 3 and q.shape[-1] == HEAD_DIM, lambda: f"q must be [total_q, H, {HEAD_DIM}], got {q.shape}")
+    torch._check(k.shape == v.shape and k.dim() == 3 and k.shape[-1] == HEAD_DIM and k.shape[1] >= 1
+                 and q.shape[1] % k.shape[1] == 0,
+                 lambda: f"k, v must be [total_k, H_kv, {HEAD_DIM}] with H_kv dividing q's heads, got {k.shape}")
+    torch._check(all(x.dtype == torch.bfloat16 for x in (q, k, v)), lambda: "q, k, v must be bfloat16")
+    torch._check(cu_q.dtype == torch.int32 and cu_k.dtype == torch.int32 and cu_q.dim() == 1
+                 and cu_q.shape == cu_k.shape and cu_q.shape[0] >= 2,
+                 lambda: "cu_seqlens_q / cu_seqlens_k must be int32 [batch + 1]")
+    torch._check(1 <= max_sq <= q.shape[0] and 1 <= max_sk <= k.shape[0],
+                 lambda: f"max_sq / max_sk must be in [1, total], got {max_sq}, {max_sk}")
+
+
+@torch.library.custom_op("fav4::varlen_forward", mutates_args=(), device_types="cuda")
+def varlen_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                   cu_seqlens_k: torch.Tensor, max_sq: int, max_sk: int, causal: bool,
+                   scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Packed sequences (fav4_bshd_forward_varlen): q [total_q, H, 128], k, v
+    [total_k, H_kv, 128], device int32 offsets [batch + 1]. Returns O (q's shape)
+    and LSE (FP32 [H, total_q]). max_sq / max_sk bound every sequence's length."""
+    _check_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_sq, max_sk)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    o = torch.empty_like(q)
+    lse = torch.empty((q.shape[1], q.shape[0]), device=q.device, dtype=torch.float32)
+    sc = 1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale
+    with torch.cuda.device(q.device):
+        _runner().call_varlen(q, k, v, o, lse, cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous(), max_sq, causal,
+                              0, sc)
+    return o, lse
+
+
+@varlen_forward.register_fake
+def _(q, k, v, cu_seqlens_q, cu_seqlens_k, max_sq, max_sk, causal, scale):
+    _check_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_sq, max_sk)
+    return torch.empty_like(q, memory_format=torch.contiguous_format), q.new_empty((q.shape[1], q.shape[0]),
+                                                                                   dtype=torch.float32)
+
+
+def _varlen_setup_context(ctx, inputs, output):
+    q, k, v, cu_q, cu_k, max_sq, max_sk, causal, scale = inputs
+    o, lse = output
+    ctx.save_for_backward(q, k, v, o, lse, cu_q, cu_k)
+    ctx.max_sq, ctx.max_sk, ctx.causal = max_sq, max_sk, causal
+    ctx.scale = 1 / math.sqrt(HEAD_DIM) if scale <= 0 else scale
+    ctx.set_materialize_grads(False)
+
+
+def _varlen_backward(ctx, grad_o, grad_lse):
+    q, k, v, o, lse, cu_q, cu_k = ctx.saved_tensors
+    if grad_lse is not None:
+        raise NotImplementedError("fav4::varlen_forward: the gradient through the LSE output is not implemented")
+    if grad_o is None:
+        return (None,) * 9
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    with torch.cuda.device(q.device):
+        _runner().backward_varlen(q.contiguous(), k.contiguous(), v.contiguous(), o, grad_o.contiguous(), lse, dq,
+                                  dk, dv, cu_q.contiguous(), cu_k.contiguous(), ctx.max_sq, ctx.max_sk, ctx.causal,
+                                  ctx.scale)
+    return dq, dk, dv, None, None, None, None, None, None
+
+
+varlen_forward.register_autograd(_varlen_backward, setup_context=_varlen_setup_context)
+
+
+def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_sq: int, max_sk: int, causal: bool = False,
+                     scale: float | None = None, return_lse: bool = False):
+    """O, or (O, LSE) when ``return_lse``, of packed sequences; differentiable in q, k, v."""
+    o, lse = torch.ops.fav4.varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_sq, max_sk, causal,
+                                           -1.0 if scale is None else scale)
+    return (o, lse) if return_lse else o
 
 
 def attention(q, k, v, causal: bool = False, config: int = 0, scale: float | None = None,

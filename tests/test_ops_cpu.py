@@ -44,3 +44,21 @@ def test_fake_rejects_invalid(case):
             config = 4
         with pytest.raises(RuntimeError):
             torch.ops.fav4.bshd_forward(q, k, v, False, config, -1.0, False)
+
+
+def test_varlen_schema_and_fake_shapes():
+    schema = str(torch.ops.fav4.varlen_forward.default._schema)
+    assert schema.startswith("fav4::varlen_forward(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens_q, "
+                             "Tensor cu_seqlens_k, SymInt max_sq, SymInt max_sk, bool causal, float scale)")
+    with FakeTensorMode():
+        q = torch.empty(900, 8, 128, dtype=torch.bfloat16, device="cuda")
+        k = torch.empty(700, 2, 128, dtype=torch.bfloat16, device="cuda")
+        cu = torch.empty(4, dtype=torch.int32, device="cuda")
+        o, lse = torch.ops.fav4.varlen_forward(q, k, k, cu, cu, 400, 300, True, -1.0)
+        assert o.shape == q.shape and lse.shape == (8, 900) and lse.dtype == torch.float32
+        with pytest.raises(RuntimeError):  # max_sq beyond total_q
+            torch.ops.fav4.varlen_forward(q, k, k, cu, cu, 901, 300, True, -1.0)
+        with pytest.raises(RuntimeError):  # heads not divisible
+            torch.ops.fav4.varlen_forward(q, torch.empty(700, 3, 128, dtype=torch.bfloat16, device="cuda"),
+                                          torch.empty(700, 3, 128, dtype=torch.bfloat16, device="cuda"), cu, cu, 400,
+                                          300, True, -1.0)

@@ -116,3 +116,35 @@ def test_gradient_limits_raise():
     o, lse = ops.attention(qg, k, v, return_lse=True)
     with pytest.raises(NotImplementedError):
         (o.float().sum() + lse.sum()).backward()
+
+
+def test_varlen_op_and_gradients_match_c_abi(runner):
+    lens_q, lens_k, h, hk = (129, 0, 700, 64), (200, 50, 900, 1), 8, 2
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    q = torch.randn((sum(lens_q), h, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    k, v = (torch.randn((sum(lens_k), hk, 128), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    do = torch.randn_like(q)
+    cu = lambda lens: torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device="cuda", dtype=torch.int32)  # noqa
+    cu_q, cu_k = cu(lens_q), cu(lens_k)
+    for causal in (False, True):
+        qg, kg, vg = (x.clone().requires_grad_(True) for x in (q, k, v))
+        o, lse = ops.varlen_attention(qg, kg, vg, cu_q, cu_k, max(lens_q), max(lens_k), causal, return_lse=True)
+        o.backward(do)
+        want_o, want_l = torch.empty_like(q), torch.empty((h, q.shape[0]), device="cuda")
+        runner.call_varlen(q, k, v, want_o, want_l, cu_q, cu_k, max(lens_q), causal)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        runner.backward_varlen(q, k, v, want_o, do, want_l, dq, dk, dv, cu_q, cu_k, max(lens_q), max(lens_k), causal)
+        torch.cuda.synchronize()
+        assert torch.equal(o.detach(), want_o) and torch.equal(lse.detach(), want_l)
+        assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
+        assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_varlen_opcheck():
+    gen = torch.Generator(device="cuda").manual_seed(32)
+    q = torch.randn((300, 4, 128), generator=gen, device="cuda", dtype=torch.bfloat16)
+    k, v = (torch.randn((260, 4, 128), generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    cu_q = torch.tensor([0, 100, 300], device="cuda", dtype=torch.int32)
+    cu_k = torch.tensor([0, 60, 260], device="cuda", dtype=torch.int32)
+    torch.library.opcheck(torch.ops.fav4.varlen_forward.default, (q, k, v, cu_q, cu_k, 200, 200, True, -1.0),
+                          test_utils=("test_schema", "test_faketensor", "test_autograd_registration"))
