@@ -448,8 +448,10 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// D = rowsum(dO * O) in FP32 and LSE * log2(e), one warp per (batch, row, head),
-// stored [B, H, stat_stride]; entries of rows sq .. stat_stride-1 are set to 0.
+// D = rowsum(dO * O) in FP32 and LSE * log2(e), stored [B, H, stat_stride]; entries of rows
+// sq .. stat_stride-1 are set to 0. Rows are (batch, query row, head) in memory order, 256 bytes
+// each; a warp takes two adjacent rows per iteration, 16 bytes of O and dO per lane (half a warp
+// per row), so one load instruction covers 512 contiguous bytes.
 __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o,
                                                             const __nv_bfloat16* __restrict__ dout,
                                                             const float* __restrict__ lse, float* __restrict__ dsum,
@@ -465,24 +467,27 @@ __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16*
   }
   const int64_t rows = static_cast<int64_t>(batch) * sq * heads;
   const int lane = threadIdx.x % 32;
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < rows;
+  const int half = lane / 16, sub = lane % 16;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; 2 * w < rows;
        w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
-    const uint2 a = reinterpret_cast<const uint2*>(o + w * kHeadDim)[lane];
-    const uint2 g = reinterpret_cast<const uint2*>(dout + w * kHeadDim)[lane];
-    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+    const int64_t row = 2 * w + half;  // (b * sq + r) * heads + h
     float s = 0.f;
+    if (row < rows) {
+      const uint4 a = reinterpret_cast<const uint4*>(o + row * kHeadDim)[sub];
+      const uint4 g = reinterpret_cast<const uint4*>(dout + row * kHeadDim)[sub];
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
-      s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
+        s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+      }
     }
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
-    if (lane == 0) {
-      // w = (b * sq + r) * heads + h  ->  D[b, h, r]
-      const int h = static_cast<int>(w % heads);
-      const int64_t br = w / heads;
+    for (int d = 8; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);  // within each half
+    if (sub == 0 && row < rows) {
+      const int h = static_cast<int>(row % heads);
+      const int64_t br = row / heads;
       const int r = static_cast<int>(br % sq);
       const int64_t bb = br / sq;
       const int64_t at = (bb * heads + h) * stat_stride + r;  // padded statistics row

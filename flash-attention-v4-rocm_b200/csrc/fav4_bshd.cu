@@ -730,7 +730,7 @@ int bwd_prepare(const Fav4BwdArgs* a, int kv_heads, int causal, void* workspace,
   st->dsum = static_cast<float*>(workspace);
   st->lse2 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + bwd_stat_bytes(a));
   const int64_t rows = static_cast<int64_t>(a->batch) * a->sq * a->heads;
-  const int64_t want = (rows + 7) / 8;
+  const int64_t want = (rows + 15) / 16;  // two rows per warp, eight warps per block
   const int64_t cap = static_cast<int64_t>(st->info.sms) * 16;
   attn_bwd_dsum_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, st->dsum,
