@@ -166,3 +166,17 @@ def test_gqa_with_group_one_equals_mha(runner):
     torch.cuda.synchronize()
     assert st == 0
     assert torch.equal(dq, mha[0]) and torch.equal(dk, mha[1]) and torch.equal(dv, mha[2])
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_backward_peaky_softmax(runner, causal, deterministic):
+    # scale 0.5 and Q x 4: logits of several hundred, rows dominated by a few keys (the regime of
+    # the edge configuration's large-logit pattern); both paths against torch autograd in FP32
+    q, k, v, do = _inputs(2, 3, 333, 517, seed=41)
+    q = (q.float() * 4).to(torch.bfloat16)
+    got = _run(runner, q, k, v, do, causal, 0.5, deterministic)
+    want = _torch_grads(q, k, v, do, causal, 0.5)
+    for g, w, n in zip(got, want, ("dq", "dk", "dv")):
+        _check(g, w, n)
+    assert runner.pipeline_status() == 0
