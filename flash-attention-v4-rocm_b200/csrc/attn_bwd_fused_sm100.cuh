@@ -12,13 +12,13 @@
 //   dV += P^T dO_i           dK += dS^T Q_i                    (TMEM, whole loop)
 //   dQ_i(j) = dS K_j                                           (TMEM, per step)
 //
-// dS goes to shared memory once, keys as rows and queries contiguous (128-byte
-// swizzle, two 64-query boxes): the K-major A operand of dK = dS^T Q_i and the
-// MN-major A operand of dQ = dS K_j.
-//
 // and adds dQ_i(j) into an FP32 accumulator with vector reductions
 // (`red.global.add.v4.f32`); a separate pass scales and converts the
 // accumulator to BF16. Five GEMMs per (i, j) pair, one exponential pass.
+//
+// dS goes to shared memory once, keys as rows and queries contiguous (128-byte
+// swizzle, two 64-query boxes): the K-major A operand of dK = dS^T Q_i and the
+// MN-major A operand of dQ = dS K_j.
 //
 // Roles (16 warps, 512 threads):
 //   warps 0-7   elementwise. Warp w serves TMEM lanes 32 (w % 4) .. +31 (keys)

@@ -1,19 +1,21 @@
 // BF16 attention backward for B200 (sm_100a), BSHD layout, head dim 128.
 //
 // The reference implements only the forward pass (README.md:24). These
-// kernels compute dQ, dK, dV of O = softmax(Q K^T * scale) V (top-left causal
-// or dense) from Q, K, V, O, dO and the forward's LSE, with the standard
-// recomputation formulas (no attention matrix in HBM, no atomics, results
-// deterministic):
+// kernels are the deterministic backward path (fav4_bshd_backward_deterministic;
+// the fused kernel in attn_bwd_fused_sm100.cuh is the default). They compute
+// dQ, dK, dV of O = softmax(Q K^T * scale) V (top-left causal or dense) from
+// Q, K, V, O, dO and the forward's LSE, with the standard recomputation
+// formulas (no attention matrix in HBM, no atomics, results deterministic):
 //
 //   P = exp(S - LSE), S = scale Q K^T     D = rowsum(dO * O)   (preprocess)
 //   dV = P^T dO     dP = dO V^T     dS = P * (dP - D)
 //   dK = scale dS^T Q                   dQ = scale dS K
 //
 // One kernel template, two modes:
-//   KV mode: a work tile is (batch, head, 128 keys); K_j and V_j stay in
-//            shared memory while the loop runs over the query tiles i that
-//            see them: S^T = K_j Q_i^T and dP^T = V_j dO_i^T (TMEM), then per
+//   KV mode: a work tile is (batch, K/V head, 128 keys); K_j and V_j stay in
+//            shared memory while the loop runs over each query head of the
+//            K/V head's group and the query tiles i that see them
+//            (bwd_step): S^T = K_j Q_i^T and dP^T = V_j dO_i^T (TMEM), then per
 //            key (TMEM lane) P^T and dS^T, then dV += P^T dO_i and
 //            dK += dS^T Q_i, accumulated in TMEM for the whole loop.
 //   Q mode:  a work tile is (batch, head, 128 query rows); Q_i and dO_i stay,
@@ -36,8 +38,8 @@
 namespace fav4 {
 
 struct BwdParams {
-  const float* lse2;  // forward LSE * log2(e) [B, H, Sq] (written by the preprocess)
-  const float* dsum;  // D = rowsum(dO * O) [B, H, Sq]
+  const float* lse2;  // forward LSE * log2(e) [B, H, stat_stride] (written by the preprocess)
+  const float* dsum;  // D = rowsum(dO * O) [B, H, stat_stride]
   __nv_bfloat16* g0;  // KV mode: dK, Q mode: dQ  ([B, S, H, 128])
   __nv_bfloat16* g1;  // KV mode: dV
   int batch, heads, sq, sk;
