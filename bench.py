@@ -604,7 +604,7 @@ def main():
     ap.add_argument("--long-context", action="store_true",
                     help="BASELINE configs[4]: B1 H8 causal split-KV across the torchrun ranks")
     ap.add_argument("--lc-seq", type=int, default=131072)
-    ap.add_argument("--e2e-chunks", type=int, default=8, help="batch chunks of the host-buffer pipeline")
+    ap.add_argument("--e2e-chunks", type=int, default=32, help="batch chunks of the host-buffer pipeline (clamped to B)")
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
