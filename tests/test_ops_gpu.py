@@ -12,6 +12,14 @@ from fav4_bshd import ops
 pytestmark = pytest.mark.gpu
 
 
+def dq_close(got, want):
+    """dQ of the fused path against another run: FP32 reductions in a different order move a
+    BF16 value by at most one ulp (rtol 2^-7), and where partial sums cancel, by up to about
+    1e-5 of the gradient's largest magnitude (atol)."""
+    g, w = got.float(), want.float()
+    return torch.allclose(g, w, rtol=2 ** -7, atol=1e-4 * w.abs().max().item() + 1e-6)
+
+
 def _inputs(b, h, sq, sk, seed):
     gen = torch.Generator(device="cuda").manual_seed(seed)
     return [torch.randn(s, generator=gen, device="cuda", dtype=torch.bfloat16)
@@ -84,7 +92,7 @@ def test_gradients_through_the_operator(runner):
     assert torch.equal(o.detach(), o2)
     assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
     # dQ is summed by FP32 atomic reductions: the order, and so the last bit, may differ between runs
-    assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
+    assert dq_close(qg.grad, dq)
 
 
 def test_gqa_gradients_through_the_operator(runner):
@@ -103,7 +111,7 @@ def test_gqa_gradients_through_the_operator(runner):
     torch.cuda.synchronize()
     assert torch.equal(o.detach(), o2)
     assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
-    assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
+    assert dq_close(qg.grad, dq)
 
 
 def test_gradient_limits_raise():
@@ -137,7 +145,7 @@ def test_varlen_op_and_gradients_match_c_abi(runner):
         torch.cuda.synchronize()
         assert torch.equal(o.detach(), want_o) and torch.equal(lse.detach(), want_l)
         assert torch.equal(kg.grad, dk) and torch.equal(vg.grad, dv)
-        assert torch.allclose(qg.grad.float(), dq.float(), rtol=2 ** -7, atol=1e-6)
+        assert dq_close(qg.grad, dq)
 
 
 def test_varlen_opcheck():
