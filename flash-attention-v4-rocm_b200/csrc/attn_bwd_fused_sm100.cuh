@@ -612,37 +612,28 @@ __global__ void __launch_bounds__(256) attn_bwd_dq_convert_kernel(const float* _
 
 // Packed sequences: D = rowsum(dO * O) and LSE * log2(e) into [B, H, stat_stride] (batch entry b's
 // row r from packed row cu_q[b] + r; 0 past the entry's length, at most max_sq), from O, dO
-// [total_q, H, 128] and the forward's LSE [H, total_q]. One warp per (b, r, h).
+// [total_q, H, 128] and the forward's LSE [H, total_q]. Two (b, r, h) slots per warp, half a warp
+// each, with the same per-row arithmetic as attn_bwd_dsum_kernel (row_dot_half).
 __global__ void __launch_bounds__(256) attn_bwd_dsum_varlen_kernel(
     const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
     float* __restrict__ dsum, float* __restrict__ lse2, const int* __restrict__ cu_q, int batch, int heads,
     int total_q, int max_sq, int stat_stride) {
   const int64_t slots = static_cast<int64_t>(batch) * stat_stride * heads;
   const int lane = threadIdx.x % 32;
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < slots;
+  const int half = lane / 16, sub = lane % 16;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; 2 * w < slots;
        w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
-    const int h = static_cast<int>(w % heads);
-    const int64_t br = w / heads;
+    const int64_t slot = 2 * w + half;  // (b * stat_stride + r) * heads + h
+    const bool in = slot < slots;
+    const int h = static_cast<int>(slot % heads);
+    const int64_t br = slot / heads;
     const int r = static_cast<int>(br % stat_stride);
-    const int b = static_cast<int>(br / stat_stride);
+    const int b = static_cast<int>(min(br / stat_stride, static_cast<int64_t>(batch - 1)));
     const int qa = min(max(__ldg(cu_q + b), 0), total_q), qe = min(max(__ldg(cu_q + b + 1), qa), total_q);
-    const bool live = r < min(qe - qa, max_sq);
-    float s = 0.f;
-    if (live) {
-      const int64_t row = (static_cast<int64_t>(qa) + r) * heads + h;
-      const uint2 a = reinterpret_cast<const uint2*>(o + row * kHeadDim)[lane];
-      const uint2 g = reinterpret_cast<const uint2*>(dout + row * kHeadDim)[lane];
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
-        s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
-      }
-#pragma unroll
-      for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
-    }
-    if (lane == 0) {
+    const bool live = in && r < min(qe - qa, max_sq);
+    const int64_t row = live ? (static_cast<int64_t>(qa) + r) * heads + h : 0;
+    const float s = row_dot_half(o + row * kHeadDim, dout + row * kHeadDim, sub, live);
+    if (sub == 0 && in) {
       const int64_t at = (static_cast<int64_t>(b) * heads + h) * stat_stride + r;
       dsum[at] = s;
       lse2[at] = live ? lse[static_cast<int64_t>(h) * total_q + qa + r] * 1.4426950408889634f : 0.f;

@@ -450,6 +450,29 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// D of one row (128 BF16 of O and of dO) over half a warp: lane `sub` (0-15) of the half takes
+// elements 8 sub .. 8 sub + 7 (nothing when `live` is false); every lane of the half ends with the
+// sum. All 32 lanes must call it together. Both preprocess kernels use it, so D is bit-identical
+// between the padded-batch and the packed-sequence layouts.
+__device__ __forceinline__ float row_dot_half(const __nv_bfloat16* o_row, const __nv_bfloat16* g_row, int sub,
+                                              bool live) {
+  float s = 0.f;
+  if (live) {
+    const uint4 a = reinterpret_cast<const uint4*>(o_row)[sub];
+    const uint4 g = reinterpret_cast<const uint4*>(g_row)[sub];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
+      s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+    }
+  }
+#pragma unroll
+  for (int d = 8; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);  // within each half
+  return s;
+}
+
 // D = rowsum(dO * O) in FP32 and LSE * log2(e), stored [B, H, stat_stride]; entries of rows
 // sq .. stat_stride-1 are set to 0. Rows are (batch, query row, head) in memory order, 256 bytes
 // each; a warp takes two adjacent rows per iteration, 16 bytes of O and dO per lane (half a warp
@@ -473,21 +496,9 @@ __global__ void __launch_bounds__(256) attn_bwd_dsum_kernel(const __nv_bfloat16*
   for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; 2 * w < rows;
        w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
     const int64_t row = 2 * w + half;  // (b * sq + r) * heads + h
-    float s = 0.f;
-    if (row < rows) {
-      const uint4 a = reinterpret_cast<const uint4*>(o + row * kHeadDim)[sub];
-      const uint4 g = reinterpret_cast<const uint4*>(dout + row * kHeadDim)[sub];
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 x = __bfloat1622float2(a2[e]), y = __bfloat1622float2(g2[e]);
-        s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
-      }
-    }
-#pragma unroll
-    for (int d = 8; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);  // within each half
-    if (sub == 0 && row < rows) {
+    const bool live = row < rows;
+    const float s = row_dot_half(o + (live ? row : 0) * kHeadDim, dout + (live ? row : 0) * kHeadDim, sub, live);
+    if (sub == 0 && live) {
       const int h = static_cast<int>(row % heads);
       const int64_t br = row / heads;
       const int r = static_cast<int>(br % sq);

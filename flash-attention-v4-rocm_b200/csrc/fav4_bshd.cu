@@ -909,7 +909,7 @@ extern "C" int fav4_bshd_backward_varlen(const Fav4VarlenBwdArgs* a, int causal,
   float* acc = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 2 * fav4::varlen_stat_bytes(a));
   {
     const int64_t slots = static_cast<int64_t>(a->batch) * stat_stride * a->heads;
-    const int64_t want = (slots + 7) / 8;
+    const int64_t want = (slots + 15) / 16;  // two slots per warp, eight warps per block
     const int64_t cap = static_cast<int64_t>(info.sms) * 16;
     fav4::attn_bwd_dsum_varlen_kernel<<<static_cast<int>(want < cap ? want : cap), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(a->o), static_cast<const __nv_bfloat16*>(a->dout), a->lse, dsum, lse2,
