@@ -4,27 +4,38 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
 
-Workload: B=32, H=8, Sq=Sk=4096, D=128, BSHD
-contiguous, Q/K/V BF16 N(0,1) (torch RNG, seed 1 + rank), scale 1/sqrt(128),
-LSE off, O buffers reused. One step = one dense and one top-left causal
-forward through the C ABI (fav4_bshd_forward), i.e. the reference's two
-headline cases. FLOPs use the reference's convention (benchmarks/bshd.py:168-
-170): dense 4*B*H*D*S^2, causal 4*B*H*D*S(S+1)/2.
+Workload: global B=32, H=8, Sq=Sk=4096, D=128, BSHD
+contiguous, Q/K/V BF16 N(0,1) (torch RNG, seed 1), scale 1/sqrt(128), LSE
+off, O buffers reused. One step = one dense and one top-left causal forward
+through the C ABI (fav4_bshd_forward), i.e. the reference's two headline
+cases. FLOPs use the reference's convention (benchmarks/bshd.py:168-170):
+dense 4*B*H*D*S^2, causal 4*B*H*D*S(S+1)/2.
 
-Multi-GPU: one process per GPU; each rank runs the same per-GPU workload on
-its own shard of a global batch of 32*N (batch sharding needs no collective),
-so scaling is weak. Timing: W warm-up steps, then exactly K steps between a
-barrier + synchronize on both sides, CUDA events on the launching stream, max
-over ranks. Inputs (1 GiB per GPU) exceed the 126 MB L2, so no flush is needed.
+Multi-GPU: one process per GPU. The global batch of 32 is sharded: rank r
+runs the unchanged C ABI on its contiguous batch slice of 32/N entries
+(batch sharding needs no collective), so scaling is strong and N=1 is the
+single-GPU headline. Timing: W warm-up steps, then exactly K steps between a
+barrier + synchronize on both sides; an L2 flush (a 256 MiB memset) runs
+before every step, outside the step's CUDA events, and a step's time is its
+first-to-last event interval on the launching stream; the max over ranks of
+the summed step times gives `value`.
 
-`value` is aggregate TFLOP/s over all ranks with inputs resident in HBM.
-`e2e` is the same metric with Q/K/V copied from pinned host memory and both
-outputs copied back inside the timed region, through fav4_bshd_forward_host
-(copies in both directions and the kernels overlapped over batch chunks).
-`roofline` relates the dense
-kernel's launches (timed with events around each launch) to the measured
-dense-BF16 peak. `cpu_baseline` (rank 0, N=1) times the FP64 CPU oracle --
-the reference's benchmarks/bshd.py:90-100 math -- on a bounded sample.
+Extra keys of the same line:
+* `e2e`: the metric with Q/K/V copied from pinned host memory and both
+  outputs copied back inside the timed region, through fav4_bshd_forward_host,
+  plus each rank's standalone host<->device copy bandwidth.
+* `roofline`: the dense kernel's launches against the measured BF16 peak.
+* `sweep`: BASELINE configs[2] (S = 512..32768, dense and causal, the global
+  B=32 sharded over the ranks) timed with the reference's graph protocol
+  (benchmarks/bshd.py:34-51,157-166): a 5-call warm-up graph, then a 20-call
+  graph replayed per observation; input sets rotate so that the bytes between
+  two reads of one set exceed the L2.
+* `long_context`: BASELINE configs[4] (B1 H8 S131072 causal): one GPU's
+  forward at N=1, the key sequence split over the ranks at N>1
+  (fav4_bshd.splitkv.SplitKV), checked against the FP64 oracle on the
+  reference's sampled rows.
+* `cpu_baseline` (rank 0, N=1): the FP64 CPU oracle -- the reference's
+  benchmarks/bshd.py:90-100 math -- on a bounded sample, on every host core.
 
 --impl reference times that same CPU oracle as the reference arm: the
 reference implementation is HIP for AMD gfx1250 and cannot run here, so the
@@ -145,13 +156,30 @@ class ClockSampler:
 
 
 # ------------------------------------------------------- CPU baseline ----
-def cpu_threads():
+def host_cores() -> int:
+    """Cores this process may run on (its CPU affinity)."""
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
-    except Exception:  # noqa: BLE001
-        return 1
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_threads_limit():
+    """Context that lets numpy's BLAS/OpenMP pools use every host core, whatever
+    OMP_NUM_THREADS the launcher set (torchrun sets 1). Yields the count."""
+    import contextlib
+
+    @contextlib.contextmanager
+    def ctx():
+        import numpy  # noqa: F401 - loads the BLAS the pools belong to
+        n = host_cores()
+        try:
+            from threadpoolctl import threadpool_limits
+            with threadpool_limits(limits=n):
+                yield n
+        except ImportError:
+            yield 1
+    return ctx()
 
 
 def cpu_sample(budget_s: float, seed: int = 1, rows_per_slice: int | None = None):
@@ -192,9 +220,14 @@ def emit(obj):
 
 
 def run_reference_arm(args, rank, world):
-    """The reference arm: the CPU oracle, rank 0 only."""
+    """The reference arm: the CPU oracle, rank 0 only, on every host core."""
     if rank != 0:
         return
+    with cpu_threads_limit() as cores:
+        _reference_arm(args, world, cores)
+
+
+def _reference_arm(args, world, cores):
     # size each step so (W + K) steps take about two minutes in total
     per_step = max(0.2, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
     rows = S
@@ -213,14 +246,14 @@ def run_reference_arm(args, rank, world):
         descs.append(d)
     wall = time.perf_counter() - t0
     value = statistics.mean(vals)
-    cores = cpu_threads()
     sample = (f"per step: one dense + one causal (b,h) slice of B32 H8 S4096 with {rows} of {S} query rows, "
               f"FP64 numpy oracle of benchmarks/bshd.py:90-100; the reference's kernel is HIP for gfx1250")
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
           "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True,
-          "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+          "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
           "config": {"workload": "B32 H8 Sq=Sk=4096 D128 BSHD dense+causal (BASELINE configs[1]); CPU sample",
-                     "batch_per_gpu": B, "heads": H, "seq_len": S, "head_dim": D, "lse": False},
+                     "global_batch": B, "heads": H, "seq_len": S, "head_dim": D, "lse": False,
+                     "cpu_threads": cores},
           "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
           "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
@@ -605,6 +638,8 @@ def main():
                     help="BASELINE configs[4]: B1 H8 causal split-KV across the torchrun ranks")
     ap.add_argument("--lc-seq", type=int, default=131072)
     ap.add_argument("--e2e-chunks", type=int, default=32, help="batch chunks of the host-buffer pipeline (clamped to B)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the configs[2] sweep key")
+    ap.add_argument("--no-long-context", action="store_true", help="skip the configs[4] long-context key")
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
@@ -637,7 +672,250 @@ def main():
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
+    run_bench(args, rank, world, local)
 
+
+# ------------------------------------------------------------ the bench ----
+L2_FLUSH_BYTES = 256 << 20  # twice the 126 MB L2
+
+
+def shard(world, rank, total=None):
+    """Batch entries [b0, b1) of the global batch owned by `rank`."""
+    total = B if total is None else total
+    if total % world:
+        raise SystemExit(f"global batch {total} is not divisible by {world} GPUs")
+    per = total // world
+    return rank * per, (rank + 1) * per
+
+
+def global_inputs(dev, b0, b1, b, s, seed):
+    """The global problem's Q/K/V drawn with one seed on every rank (so the
+    shards of all ranks form the same global batch N=1 computes), sliced to
+    this rank's batch entries."""
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    out = []
+    for _ in range(3):
+        full = torch.randn((b, s, H, D), generator=gen, device=dev, dtype=torch.bfloat16)
+        out.append(full[b0:b1].clone())
+        del full
+    return out
+
+
+def timed_steps(step, steps, stream, flush):
+    """Run `steps` steps, each after an L2 flush; returns the per-step
+    first-to-last event intervals (ms) and the per-launch intervals."""
+    import torch
+    evs = []
+    for _ in range(steps):
+        flush()
+        ev = step(True)
+        evs.append(ev)
+    torch.cuda.synchronize()
+    per_step = [ev[0].elapsed_time(ev[-1]) for ev in evs]
+    per_launch = [[ev[i].elapsed_time(ev[i + 1]) for i in range(len(ev) - 1)] for ev in evs]
+    return per_step, per_launch
+
+
+def max_over_ranks(vals, world, dev):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def gather_ranks(vals, world, dev):
+    """[world][len(vals)] from every rank's list (same length on every rank)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world == 1:
+        return [t.tolist()]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [x.tolist() for x in out]
+
+
+def sweep_key(args, runner, world, rank, dev, barrier):
+    """BASELINE configs[2] with the reference's graph protocol
+    (benchmarks/bshd.py:34-51,157-166): per (S, mask) a CUDA graph of 5 calls
+    (warm-up) and one of 20 calls; an observation replays the warm-up graph,
+    synchronises, and times one replay of the 20-call graph with CUDA events.
+    Observations: 6 up to S=4096, 3 at 8192, 2 above (bounded bench time).
+    The global B=32 is sharded over the ranks; input sets (Q, K, V, O) rotate
+    through the graph's calls so that more than 256 MiB is touched between two
+    reads of one set (inputs larger than L2). Per point: the max over ranks of
+    the median per-call time, the aggregate TFLOP/s it gives, and the per-GPU
+    fraction of the measured peak."""
+    import torch
+    pk, pk_kind = peaks()
+    b0, b1 = shard(world, rank)
+    nb = b1 - b0
+    stream = torch.cuda.current_stream()
+    points = []
+    for n in [int(x) for x in args.seqs.split(",")]:
+        set_bytes = 4 * nb * n * H * D * 2
+        sets = max(1, -(-L2_FLUSH_BYTES // set_bytes))
+        data = []
+        for i in range(sets):
+            q, k, v = global_inputs(dev, b0, b1, B, n, 2 + 1000 * i)
+            data.append((q, k, v, torch.empty_like(q)))
+        obs = 6 if n <= 4096 else (3 if n <= 8192 else 2)
+        for causal in (False, True):
+            def calls(count, causal=causal):
+                for c in range(count):
+                    q, k, v, o = data[c % sets]
+                    runner.call(q, k, v, o, None, causal, args.config)
+            calls(2)  # one-time attribute set-up outside capture
+            torch.cuda.synchronize()
+            warm, timed = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(warm):
+                calls(5)
+            with torch.cuda.graph(timed):
+                calls(20)
+            us = []
+            barrier()
+            for _ in range(obs):
+                warm.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                timed.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                us.append(e0.elapsed_time(e1) * 1e3 / 20)
+            del warm, timed
+            med = statistics.median(us)
+            worst = max_over_ranks([med], world, dev)[0]
+            f = flops(B, H, n, causal)
+            tf = f / worst / 1e6
+            points.append({"seq": n, "causal": causal, "us_per_call": worst, "tflops": tf,
+                           "tflops_per_gpu": tf / world, "frac_of_measured_bf16_per_gpu": tf / world / pk["bf16_tflops"],
+                           "gbs_per_gpu": set_bytes / worst / 1e3,
+                           "frac_of_measured_hbm_per_gpu": set_bytes / worst / 1e3 / pk["hbm_gbs"],
+                           "observations": obs, "input_sets": sets})
+        del data
+        torch.cuda.empty_cache()
+    work_tiles = {p["seq"]: nb * H * -(-p["seq"] // 256) for p in points if not p["causal"]}
+    return {"points": points, "global_batch": B, "batch_per_gpu": nb, "heads": H, "head_dim": D,
+            "protocol": "reference graph protocol: 5-call warm-up graph, 20-call timed graph, median of "
+                        "observations, max over ranks", "peak_source": pk_kind,
+            "work_tiles_per_gpu_of_256_rows": work_tiles,
+            "limiter_note": "per GPU the kernel walks batch_per_gpu*8*ceil(S/256) work tiles over 148 SMs; at "
+                            "short S and small per-GPU batches the last wave and the per-tile pipeline fill "
+                            "and drain bound the rate"}
+
+
+def long_context_key(args, world, rank, local, dev, barrier):
+    """B1 H8 S131072 causal, LSE on, seed 4. N=1: one
+    forward of the whole problem; N>1: the key sequence split over the ranks
+    (zigzag chunks, NVLink combine). Timed over K steps after W warm-up steps
+    (device events, max over ranks); the output rows the reference's benchmark
+    samples (benchmarks/bshd.py:147-148) are gathered to rank 0 and checked
+    against the FP64 oracle."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import fav4_bshd
+    from oracle import ref_attention as R
+    b, h, n = 1, H, args.lc_seq
+    gen = torch.Generator(device=dev).manual_seed(4)  # same inputs on every rank
+    q, k, v = (torch.randn((b, n, h, D), generator=gen, device=dev, dtype=torch.bfloat16) for _ in range(3))
+    if world > 1:
+        from fav4_bshd.splitkv import SplitKV
+        skv = SplitKV(dist.group.WORLD, b, h, n, n, dev)
+        r0, r1 = skv.r0, skv.r1
+
+        def fwd():
+            return skv.forward(q, k, v, True, args.config)
+    else:
+        runner = fav4_bshd.Runner()
+        o_full = torch.empty_like(q)
+        l_full = torch.empty((b, h, n), device=dev, dtype=torch.float32)
+        r0, r1 = 0, n
+
+        def fwd():
+            runner.call(q, k, v, o_full, l_full, True, args.config)
+            return o_full, l_full
+    lc_steps, lc_warm = max(2, min(5, args.steps)), 2
+    for _ in range(lc_warm):
+        fwd()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(lc_steps):
+        o, lse = fwd()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks([e0.elapsed_time(e1) / lc_steps], world, dev)[0]
+    # sampled rows: each rank contributes the rows it owns, rank 0 checks them
+    rows = R.sample_rows(n)
+    got_o = torch.zeros((len(rows), h, D), device=dev, dtype=torch.float32)
+    got_l = torch.zeros((h, len(rows)), device=dev, dtype=torch.float32)
+    for i, r in enumerate(rows.tolist()):
+        if r0 <= r < r1:
+            got_o[i] = o[0, r - r0].float()
+            got_l[:, i] = lse[0, :, r - r0]
+    if world > 1:
+        dist.all_reduce(got_o)
+        dist.all_reduce(got_l)
+    f = flops(b, h, n, True)
+    out = {"workload": f"B1 H8 Sq=Sk={n} D128 causal, LSE on, seed 4 (BASELINE configs[4])",
+           "mode": "one GPU forward" if world == 1 else f"key sequence split over {world} GPUs (zigzag, NVLink combine)",
+           "ms_per_step": ms, "tflops": f / (ms * 1e-3) / 1e12, "tflops_per_gpu": f / (ms * 1e-3) / 1e12 / world,
+           "steps": lc_steps, "warmup": lc_warm}
+    if rank == 0:
+        with cpu_threads_limit():
+            qn = np.zeros((1, n, h, D), dtype=np.float32)
+            qn[0, rows] = q[0, torch.as_tensor(rows, device=dev)].float().cpu().numpy()
+            kn, vn = (x.float().cpu().numpy() for x in (k, v))
+            ref, ref_lse = R.reference_chunked(qn, kn, vn, True, rows)
+        go = got_o.cpu().numpy().transpose(1, 0, 2)[None].astype(np.float64)  # [1, H, rows, D]
+        gl = got_l.cpu().numpy()[None].astype(np.float64)
+        st = R.error_stats(go, gl, ref, ref_lse)
+        out["vs_fp64_sampled_rows"] = {
+            "rows": len(rows), "max_abs_o": st["max_abs"], "mean_abs_o": st["mean_abs"],
+            "max_abs_lse": st["lse_max_abs"], "reference_criteria": R.reference_criteria_pass(go, gl, ref, ref_lse),
+            "within_tolerance": bool(st["finite"] and st["max_abs"] <= 2e-2 and st["mean_abs"] <= 2e-3
+                                     and st["lse_max_abs"] <= 1e-3)}
+    if world > 1:
+        del skv
+    del q, k, v
+    torch.cuda.empty_cache()
+    return out
+
+
+def copy_bandwidth(hq, hk, hv, dev, world, stream):
+    """Each rank's standalone copy rates, all ranks at the same time: Q/K/V
+    host -> device, then two outputs device -> host (page-locked buffers)."""
+    import torch
+    dq, dk, dv = (torch.empty(x.shape, dtype=x.dtype, device=dev) for x in (hq, hk, hv))
+    ho = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
+    torch.cuda.synchronize()
+    res = []
+    for direction in ("h2d", "d2h"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(3):
+            if direction == "h2d":
+                for d, hsrc in ((dq, hq), (dk, hk), (dv, hv)):
+                    d.copy_(hsrc, non_blocking=True)
+            else:
+                ho.copy_(dq, non_blocking=True)
+                ho.copy_(dk, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        nbytes = 3 * (3 if direction == "h2d" else 2) * hq.numel() * hq.element_size()
+        res.append(nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    return gather_ranks(res, world, dev)
+
+
+def run_bench(args, rank, world, local):
     import torch
     import torch.distributed as dist
 
@@ -655,27 +933,33 @@ def main():
 
     lib = fav4_bshd.load_library()
     runner = fav4_bshd.Runner(lib)
-    gen = torch.Generator(device=dev).manual_seed(1 + rank)
-    q, k, v = (torch.randn((B, S, H, D), generator=gen, device=dev, dtype=torch.bfloat16) for _ in range(3))
+    b0, b1 = shard(world, rank)
+    nb = b1 - b0
+    q, k, v = global_inputs(dev, b0, b1, B, S, 1)
     o_dense, o_causal = torch.empty_like(q), torch.empty_like(q)
     stream = torch.cuda.current_stream()
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    def step(ev=None):
-        if ev is not None:
+    def flush():
+        flush_buf.zero_()
+
+    def step(timed=False):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if timed else None
+        if timed:
             ev[0].record(stream)
         runner.call(q, k, v, o_dense, None, False, args.config)
-        if ev is not None:
+        if timed:
             ev[1].record(stream)
         runner.call(q, k, v, o_causal, None, True, args.config)
-        if ev is not None:
+        if timed:
             ev[2].record(stream)
+        return ev
 
     for _ in range(args.warmup):
+        flush()
         step()
     torch.cuda.synchronize()
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
         nvml_index = torch.cuda._get_nvml_device_index(dev)
     except Exception:  # noqa: BLE001
@@ -683,21 +967,18 @@ def main():
     sampler = ClockSampler(nvml_index)
     barrier()
     torch.cuda.synchronize()
+    region0, region1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
-        start.record(stream)
-        for i in range(args.steps):
-            step(evs[i])
-        end.record(stream)
+        region0.record(stream)
+        per_step, per_launch = timed_steps(step, args.steps, stream, flush)
+        region1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    ms = start.elapsed_time(end)
-    dense_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    causal_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * STEP_FLOPS * args.steps / (ms_max * 1e-3) / 1e12
+    region_ms = region0.elapsed_time(region1)
+    dense_ms = [x[0] for x in per_launch]
+    causal_ms = [x[1] for x in per_launch]
+    ms_sum, region_max = max_over_ranks([sum(per_step), region_ms], world, dev)
+    value = STEP_FLOPS * args.steps / (ms_sum * 1e-3) / 1e12
 
     # ---- end to end through the C ABI with host buffers ----
     # fav4_bshd_forward_host: one upload of Q/K/V from page-locked memory,
@@ -708,9 +989,10 @@ def main():
     ho_d = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     ho_c = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     outs = [(ho_d, None, False, args.config), (ho_c, None, True, args.config)]
+    chunks = min(args.e2e_chunks, nb)
 
     def e2e_step():
-        runner.forward_host(hq, hk, hv, outs, chunks=args.e2e_chunks, stream=stream)
+        runner.forward_host(hq, hk, hv, outs, chunks=chunks, stream=stream)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -723,15 +1005,23 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * STEP_FLOPS * e2e_steps / (float(te.item()) * 1e-3) / 1e12
+    te = max_over_ranks([e0.elapsed_time(e1)], world, dev)[0]
+    e2e_value = STEP_FLOPS * e2e_steps / (te * 1e-3) / 1e12
     h2d = 3 * q.numel() * q.element_size()
     d2h = 2 * q.numel() * q.element_size()
     ok_e2e = torch.equal(ho_d, o_dense.cpu()) and torch.equal(ho_c, o_causal.cpu())
+    barrier()
+    copy_rates = copy_bandwidth(hq, hk, hv, dev, world, stream)
+    del hq, hk, hv, ho_d, ho_c
+    status_main = runner.pipeline_status(clear=False)
+    del q, k, v, o_dense, o_causal
+    torch.cuda.empty_cache()
 
+    # ---- BASELINE configs[2] sweep and configs[4] long context (extra keys) ----
+    sweep = None if args.no_sweep else sweep_key(args, runner, world, rank, dev, barrier)
+    lc = None if args.no_long_context else long_context_key(args, world, rank, local, dev, barrier)
     status = runner.pipeline_status(clear=False)
+    statuses = gather_ranks([float(status_main), float(status)], world, dev)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -739,38 +1029,53 @@ def main():
 
     pk, pk_kind = peaks()
     dense_avg = statistics.mean(dense_ms)
-    achieved = flops(B, H, S, False) / (dense_avg * 1e-3) / 1e12
-    long_region = ms_max > 2000.0
+    achieved = flops(nb, H, S, False) / (dense_avg * 1e-3) / 1e12
+    long_region = region_max > 2000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
     traffic = committed_traffic()
-    roofline = {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel (dense, config Auto=2)",
+    roofline = {"bound": "tensor", "kernel": f"attn_fwd_sm100_kernel (dense, config Auto=2), B{nb} per GPU",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16",
-                "traffic": traffic.get("dense_dram_bytes_per_launch") if traffic else None,
-                "algorithmic_flops_per_launch": flops(B, H, S, False),
-                "algorithmic_bytes_per_launch": 4 * B * S * H * D * 2,
+                "traffic": (traffic.get("dense_dram_bytes_per_launch") if traffic and nb == 32 else None),
+                "algorithmic_flops_per_launch": flops(nb, H, S, False),
+                "algorithmic_bytes_per_launch": 4 * nb * S * H * D * 2,
                 "dense_ms_median": statistics.median(dense_ms), "causal_ms_median": statistics.median(causal_ms),
                 "dense_tflops": achieved,
-                "causal_tflops": flops(B, H, S, True) / (statistics.mean(causal_ms) * 1e-3) / 1e12,
+                "causal_tflops": flops(nb, H, S, True) / (statistics.mean(causal_ms) * 1e-3) / 1e12,
                 "frac_of_nominal_2250": achieved / 2250.0}
+    h2d_rates = [r[0] for r in copy_rates]
+    d2h_rates = [r[1] for r in copy_rates]
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "warmup": args.warmup, "ms_per_step": ms_sum / args.steps, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "config": {"workload": f"B{B} H{H} Sq=Sk={S} D128 BSHD, one dense + one causal forward per step"
                                   + (" (BASELINE configs[1])" if (B, S) == (32, 4096) else " (profiling shape)"),
-                      "batch_per_gpu": B, "global_batch": B * world, "heads": H, "seq_len": S, "head_dim": D,
+                      "global_batch": B, "batch_per_gpu": nb, "heads": H, "seq_len": S, "head_dim": D,
                       "lse": False, "fav4_config": args.config,
-                      "parallelism": f"batch-sharded x{world}, no collective",
-                      "l2": "inputs 1 GiB per GPU > 126 MB L2 (no flush)"},
+                      "parallelism": f"global batch sharded over {world} GPU(s) ({nb} per GPU), no collective",
+                      "l2": "flushed before every step (256 MiB memset, outside the step's events)",
+                      "timing": "sum over steps of each step's first-to-last CUDA event interval, max over ranks",
+                      "region_ms_max_over_ranks": region_max},
            "gpu_launches": 2 * args.steps,
-           "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                   "steps": e2e_steps, "outputs_match": ok_e2e,
-                   "api": f"fav4_bshd_forward_host, {args.e2e_chunks} batch chunks, page-locked host buffers"},
-           "roofline": roofline, "clocks": sampler.summary(), "pipeline_status": status}
+           "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+                   "d2h_bytes_per_step": d2h * world, "h2d_bytes_per_step_per_gpu": h2d,
+                   "d2h_bytes_per_step_per_gpu": d2h, "steps": e2e_steps, "outputs_match": ok_e2e,
+                   "api": f"fav4_bshd_forward_host, {chunks} batch chunks per GPU, page-locked host buffers",
+                   "h2d_gbs_per_rank": h2d_rates, "d2h_gbs_per_rank": d2h_rates,
+                   "copy_bound_ms_per_step": max(h2d / (r * 1e9) * 1e3 for r in h2d_rates),
+                   "note": "h2d/d2h_gbs_per_rank: standalone copies of one step's inputs / outputs, all ranks "
+                           "at once; the e2e step cannot beat its upload time (copy_bound_ms_per_step)"},
+           "roofline": roofline, "clocks": sampler.summary(),
+           "pipeline_status": {"headline_and_e2e": int(max(r[0] for r in statuses)),
+                               "after_sweep_and_long_context": int(max(r[1] for r in statuses))}}
+    if sweep is not None:
+        out["sweep"] = sweep
+    if lc is not None:
+        out["long_context"] = lc
     if world == 1 and not args.no_cpu_baseline:
-        v_cpu, desc = cpu_sample(args.cpu_budget)
-        out["cpu_baseline"] = {"value": v_cpu, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                               "sample": desc}
+        with cpu_threads_limit() as cores:
+            v_cpu, desc = cpu_sample(args.cpu_budget)
+        out["cpu_baseline"] = {"value": v_cpu, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
     emit(out)
 
 

@@ -41,6 +41,8 @@ uint64_t wait_limit_ns() {
   return limit;
 }
 
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
 struct DeviceInfo {
   int sms = 0;
   uint32_t* status = nullptr;
@@ -77,6 +79,8 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
         reinterpret_cast<uintptr_t>(a->o)) &
        15))
     return false;
+  // LSE is written with 4-byte stores: a misaligned pointer would fault on the GPU
+  if (reinterpret_cast<uintptr_t>(a->lse) & 3) return false;
   return true;
 }
 
@@ -243,7 +247,7 @@ int combine_parts(const void* const* o_parts, const float* const* lse_parts, int
                   int batch, int heads, int sq, cudaStream_t stream) {
   if (!o_parts || !lse_parts || !o || parts < 1 || parts > kCombineCapacity || batch <= 0 || heads <= 0 ||
       sq <= 0 || batch > INT_MAX / heads || heads > INT_MAX / 128 || sq > INT_MAX / (heads * 128) ||
-      (reinterpret_cast<uintptr_t>(o) & 15))
+      (reinterpret_cast<uintptr_t>(o) & 15) || (reinterpret_cast<uintptr_t>(lse) & 3))
     return cudaErrorInvalidValue;
   CombineParams p = {};
   for (int g = 0; g < parts; ++g) {
@@ -282,75 +286,6 @@ extern "C" int fav4_bshd_combine(const void* const* o_parts, const float* const*
 }
 
 // --------------------------------------------------------------------------
-// Split-KV forward with its partials in a fixed device array (no cudaMalloc),
-// for callers that cannot allocate device memory. One array per device,
-// shared by every call: overlapping calls race (see include/fav4_bshd.h).
-namespace fav4 {
-namespace {
-
-constexpr size_t kStaticScratchBytes = size_t(64) << 20;  // 64 MiB
-static __device__ __align__(256) unsigned char g_splitkv_scratch[kStaticScratchBytes];
-
-size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
-
-// Device address of g_splitkv_scratch on the current device, looked up once
-// per device with that device current (host code cannot use the symbol itself).
-cudaError_t static_scratch(int dev, unsigned char** out) {
-  static std::mutex mu;
-  static unsigned char* addr[kMaxDevices] = {};
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_splitkv_scratch);
-    if (e != cudaSuccess) return e;
-    addr[dev] = static_cast<unsigned char*>(p);
-  }
-  *out = addr[dev];
-  return cudaSuccess;
-}
-
-}  // namespace
-}  // namespace fav4
-
-extern "C" int fav4_bshd_forward_splitkv_static(const Fav4Args* a, int causal, int config, int splits,
-                                                cudaStream_t stream) {
-  if (!fav4::args_valid(a, causal, config) || splits < 1 || splits > fav4::kMaxCombineParts)
-    return cudaErrorInvalidValue;
-  if (config == 0) config = fav4_bshd_select_config(a);
-  // Whole 128-key tiles per slice.
-  const int per = (a->sk + splits - 1) / splits;
-  const int step = ((per + fav4::kBlockN - 1) / fav4::kBlockN) * fav4::kBlockN;
-  const int parts = (a->sk + step - 1) / step;
-  const size_t rows = static_cast<size_t>(a->batch) * a->sq * a->heads;
-  const size_t o_bytes = fav4::round256(rows * fav4::kHeadDim * 2);
-  const size_t lse_bytes = fav4::round256(rows * 4);
-  if (static_cast<size_t>(parts) * (o_bytes + lse_bytes) > fav4::kStaticScratchBytes)
-    return cudaErrorMemoryAllocation;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  unsigned char* scratch = nullptr;
-  e = fav4::static_scratch(dev, &scratch);
-  if (e != cudaSuccess) return e;
-  const void* o_parts[fav4::kMaxCombineParts];
-  const float* lse_parts[fav4::kMaxCombineParts];
-  for (int g = 0; g < parts; ++g) {
-    Fav4Args pa = *a;
-    pa.o = scratch + g * o_bytes;
-    pa.lse = reinterpret_cast<float*>(scratch + parts * o_bytes + g * lse_bytes);
-    const int kv_begin = g * step;
-    const int kv_end = kv_begin + step < a->sk ? kv_begin + step : a->sk;
-    e = static_cast<cudaError_t>(causal ? fav4::dispatch<true>(pa, config, kv_begin, kv_end, stream)
-                                        : fav4::dispatch<false>(pa, config, kv_begin, kv_end, stream));
-    if (e != cudaSuccess) return e;
-    o_parts[g] = pa.o;
-    lse_parts[g] = pa.lse;
-  }
-  return fav4_bshd_combine(o_parts, lse_parts, parts, a->o, a->lse, a->batch, a->heads, a->sq, stream);
-}
-
-// --------------------------------------------------------------------------
 // Forward from host buffers, pipelined over batch chunks: the copy of chunk
 // c+1 to the device, the forwards of chunk c and the copy of chunk c-1 back
 // to the host run at the same time (two copy streams beside the caller's
@@ -385,8 +320,11 @@ bool host_layout(const Fav4Args* a, const Fav4HostOut* outs, int n_outs, int chu
   return true;
 }
 
-// Streams and events of one call, released when the call returns (the
-// runtime frees them once the work queued on them has finished).
+// Copy streams and events of fav4_bshd_forward_host, created on a device's
+// first call (with that device current) and kept until the process exits, so
+// a call creates nothing. A call holds its device's mutex while it enqueues:
+// host threads that call at the same time take turns (enqueueing only; the
+// GPU work of consecutive calls is ordered through the callers' streams).
 struct HostPipe {
   cudaStream_t up = nullptr, down = nullptr;
   cudaEvent_t fork = nullptr, uploaded[2] = {}, computed[2] = {}, downloaded[2] = {};
@@ -397,16 +335,32 @@ struct HostPipe {
                           &downloaded[1]};
     for (cudaEvent_t* ev : all)
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    if (e != cudaSuccess) release();
     return e;
   }
-  ~HostPipe() {
-    cudaEvent_t all[] = {fork, uploaded[0], uploaded[1], computed[0], computed[1], downloaded[0], downloaded[1]};
-    for (cudaEvent_t ev : all)
-      if (ev) cudaEventDestroy(ev);
+  void release() {
+    cudaEvent_t* all[] = {&fork, &uploaded[0], &uploaded[1], &computed[0], &computed[1], &downloaded[0],
+                          &downloaded[1]};
+    for (cudaEvent_t* ev : all) {
+      if (*ev) cudaEventDestroy(*ev);
+      *ev = nullptr;
+    }
     if (up) cudaStreamDestroy(up);
     if (down) cudaStreamDestroy(down);
+    up = down = nullptr;
   }
 };
+
+struct HostPipeSlot {
+  std::mutex mu;
+  HostPipe pipe;
+  bool ready = false;
+};
+
+HostPipeSlot* host_pipe_slot(int dev) {
+  static HostPipeSlot slots[kMaxDevices];
+  return (dev >= 0 && dev < kMaxDevices) ? &slots[dev] : nullptr;
+}
 
 }  // namespace
 }  // namespace fav4
@@ -428,9 +382,18 @@ extern "C" int fav4_bshd_forward_host(const Fav4Args* a, const Fav4HostOut* outs
   for (int j = 0; j < n_outs; ++j)
     if (!outs[j].o || (outs[j].causal != 0 && outs[j].causal != 1) || outs[j].config < 0 || outs[j].config > 3)
       return cudaErrorInvalidValue;
-  fav4::HostPipe pipe;
-  cudaError_t e = pipe.create();
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  fav4::HostPipeSlot* slot_of_dev = fav4::host_pipe_slot(dev);
+  if (!slot_of_dev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> pipe_lock(slot_of_dev->mu);
+  if (!slot_of_dev->ready) {
+    e = slot_of_dev->pipe.create();
+    if (e != cudaSuccess) return e;
+    slot_of_dev->ready = true;
+  }
+  fav4::HostPipe& pipe = slot_of_dev->pipe;
   // The copy streams start behind everything already queued on the caller's stream.
   e = cudaEventRecord(pipe.fork, stream);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pipe.up, pipe.fork, 0);
@@ -607,6 +570,55 @@ extern "C" int fav4_bshd_forward_partial_splitkv(const Fav4Args* a, int causal, 
   if (config == 0) config = fav4_bshd_select_config(a);
   if (splits == 1) return fav4_bshd_forward_partial(a, causal, config, kv_begin, kv_end, stream);
   return fav4::splitkv_range(a, causal, config, kv_begin, kv_end, splits, workspace, workspace_bytes, stream);
+}
+
+// --------------------------------------------------------------------------
+// Split-KV forward with its partials in a fixed device array (no cudaMalloc),
+// for callers that cannot allocate device memory. One array per device,
+// shared by every call: overlapping calls race (see include/fav4_bshd.h).
+// The slices run as one launch of the key-range kernel (splitkv_range), the
+// array standing in for the caller's workspace.
+namespace fav4 {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(64) << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_splitkv_scratch[kStaticScratchBytes];
+
+// Device address of g_splitkv_scratch on the current device, looked up once
+// per device with that device current (host code cannot use the symbol itself).
+cudaError_t static_scratch(int dev, unsigned char** out) {
+  static std::mutex mu;
+  static unsigned char* addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_splitkv_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace fav4
+
+extern "C" int fav4_bshd_forward_splitkv_static(const Fav4Args* a, int causal, int config, int splits,
+                                                cudaStream_t stream) {
+  if (!fav4::args_valid(a, causal, config) || splits < 1 || splits > fav4::kMaxCombineParts)
+    return cudaErrorInvalidValue;
+  if (config == 0) config = fav4_bshd_select_config(a);
+  if (splits == 1) return fav4_bshd_forward(a, causal, config, stream);  // one slice: no partials
+  const size_t need = fav4_bshd_splitkv_workspace_bytes(a, splits);
+  if (need == 0 || need > fav4::kStaticScratchBytes) return cudaErrorMemoryAllocation;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  unsigned char* scratch = nullptr;
+  e = fav4::static_scratch(dev, &scratch);
+  if (e != cudaSuccess) return e;
+  return fav4::splitkv_range(a, causal, config, 0, a->sk, splits, scratch, fav4::kStaticScratchBytes, stream);
 }
 
 // --------------------------------------------------------------------------

@@ -100,24 +100,31 @@ int fav4_bshd_combine(const void* const* o_parts, const float* const* lse_parts,
 
 /* Split-KV forward on one GPU that allocates nothing (no counterpart in the
  * reference). Same result as fav4_bshd_forward (within the split-KV
- * tolerance), computed as `splits` KV slices plus the LSE-weighted combine.
- * It is for callers that cannot call cudaMalloc: code that runs while a CUDA
- * graph is being captured, plugins whose host owns every byte of device
- * memory through its own pool, and latency-critical paths that cannot take
- * cudaMalloc's implicit device synchronisation. The slice partials live in a
- * fixed 64 MiB device array inside the library instead; every GPU that loads
- * the library holds that array until the process exits.
- *   - 1 <= splits <= 16; slices are whole 128-key tiles, so fewer slices are
- *     used when sk is short.
- *   - Needs slices * (batch*sq*heads*256 + batch*heads*sq*4) bytes, each part
- *     rounded up to 256 bytes; larger problems return
- *     cudaErrorMemoryAllocation (2) before anything is launched.
- *   - The first call on a device looks up the array's device address; make
- *     that first call before any stream capture.
+ * tolerance), computed as `splits` key ranges in one launch of the split-KV
+ * kernel plus the LSE-weighted combine. It is for callers that cannot call
+ * cudaMalloc: plugins whose host application owns every byte of device
+ * memory through its own pool (there a cudaMalloc fails, or takes memory the
+ * host has promised elsewhere), and latency-critical paths that cannot take
+ * cudaMalloc's implicit device synchronisation. The key-range partials live
+ * in a fixed 64 MiB device array inside the library instead; every GPU that
+ * loads the library holds that array until the process exits.
+ *   - 1 <= splits <= 16; splits = 1 is fav4_bshd_forward (no partials).
+ *   - Needs fav4_bshd_splitkv_workspace_bytes(args, splits) bytes, i.e.
+ *     splits * (batch*sq*heads*256 + batch*heads*sq*4), each part rounded up
+ *     to 256 bytes; larger problems return cudaErrorMemoryAllocation (2)
+ *     before anything is launched.
+ *   - Set-up happens on first use: the first call on a device looks up the
+ *     array's device address, and the first call of each (causal, config)
+ *     variant sets its kernel's shared-memory limit. Make one call of each
+ *     variant you use before any stream capture. The array itself is
+ *     reserved when the library's kernels are loaded on a device (with lazy
+ *     module loading, at the first launch), so make that call before a host
+ *     pool claims the device's memory as well.
  *   - All calls share the one array: calls whose work overlaps on the GPU
  *     (different streams, or different host threads) race and give wrong
  *     results. Serialise them. Every byte a call reads from the array is
- *     written earlier by the same call, so stale contents never leak.
+ *     written earlier by the same call, so nothing needs clearing and stale
+ *     contents never leak.
  * Other arguments and return codes as fav4_bshd_forward. */
 int fav4_bshd_forward_splitkv_static(const Fav4Args* args, int causal, int config, int splits,
                                      cudaStream_t stream);

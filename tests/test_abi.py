@@ -287,3 +287,23 @@ def test_varlen_rejects_invalid_arguments(lib):
     assert f(C.byref(va()), 2, 0, None) == INVALID
     assert f(C.byref(va()), 0, 5, None) == INVALID
     assert f(None, 0, 0, None) == INVALID
+
+
+def test_misaligned_lse_is_rejected_by_every_forward_entry(lib):
+    # LSE is stored with 4-byte stores; a pointer that is not 4-byte aligned
+    # would fault on the GPU, so each entry refuses it before any CUDA call.
+    for off in (1, 2, 3):
+        a = make_args(batch=1, heads=8, sq=16, sk=4096, lse=A16 * 5 + off)
+        ws = A16 * 256
+        need = lib.fav4_bshd_splitkv_workspace_bytes(C.byref(a), 4)
+        assert lib.fav4_bshd_forward(C.byref(a), 0, 0, None) == INVALID
+        assert lib.fav4_bshd_forward(C.byref(a), 1, 2, None) == INVALID
+        assert lib.fav4_bshd_forward_gqa(C.byref(a), 2, 0, 0, None) == INVALID
+        assert lib.fav4_bshd_forward_partial(C.byref(a), 0, 0, 0, 64, None) == INVALID
+        assert lib.fav4_bshd_forward_splitkv(C.byref(a), 0, 0, 4, ws, need, None) == INVALID
+        assert lib.fav4_bshd_forward_partial_splitkv(C.byref(a), 0, 0, 0, 4096, 4, ws, need, None) == INVALID
+        assert lib.fav4_bshd_forward_splitkv_static(C.byref(a), 1, 0, 4, None) == INVALID
+        assert lib.fav4_bshd_splitkv_splits(C.byref(a), 0, 0) == -1
+        o = (C.c_void_p * 2)(A16, A16 * 2)
+        lse = (C.c_void_p * 2)(A16 * 3, A16 * 4)
+        assert lib.fav4_bshd_combine(o, lse, 2, A16 * 5, C.c_void_p(A16 * 6 + off), 1, 8, 64, None) == INVALID

@@ -1,16 +1,16 @@
 """GPU test of fav4_bshd_forward_splitkv_static, the entry point that
 allocates no device memory.
 
-Some callers cannot call cudaMalloc: code running while a CUDA graph is being
-captured, plugins whose host application owns all device memory through its
-own pool, and latency-critical paths that cannot afford cudaMalloc's implicit
-device synchronisation. For them the library keeps the split-KV partials in
-a fixed 64 MiB device array of its own. This test calls that entry point
-through the C ABI twice in a row, on different problems, and checks each
-result against the existing entry point (fav4_bshd_forward) with the same
-tolerance the split-KV tests use. It also checks that a problem too large
-for the array is refused before anything runs, and that a repeated call
-leaves the device's free memory unchanged.
+Some callers cannot call cudaMalloc: plugins whose host application owns all
+device memory through its own pool (a cudaMalloc there fails or takes memory
+the host has promised elsewhere), and latency-critical paths that cannot
+afford cudaMalloc's implicit device synchronisation. For them the library
+keeps the split-KV partials in a fixed 64 MiB device array of its own. This
+test calls that entry point through the C ABI twice in a row, on different
+problems, and checks each result against the existing entry point
+(fav4_bshd_forward) with the same tolerance the split-KV tests use. It also
+checks that a problem too large for the array is refused before anything
+runs, and that a repeated call leaves the device's free memory unchanged.
 
 The file name sorts last so a run that stops at its first failure has
 already run every other test; it also passes alone in a fresh process.
