@@ -4,7 +4,8 @@
   torchrun: each rank's output rows must match a single-GPU forward of the
   whole causal problem within the north-star tolerance.
 * bench.py's batch-sharded headline run under torchrun prints one JSON line
-  with n_gpus = 2 and no pipeline timeouts.
+  with n_gpus = 2, the global batch split in two, no pipeline timeouts, and
+  its sweep and long-context keys (the latter within tolerance of FP64).
 * The decode split-KV path (fav4_bshd.splitkv.DecodeSplitKV) across 2 ranks:
   every rank's full output matches one GPU's split-KV forward.
 """
@@ -43,8 +44,13 @@ def test_long_context_split_kv_two_gpus():
 
 @needs2
 def test_batch_sharded_bench_two_gpus():
-    out = _torchrun(2, "--gpus", "2", "--steps", "3", "--warmup", "3")
-    assert out["n_gpus"] == 2 and out["pipeline_status"] == 0 and out["value"] > 0, out
+    out = _torchrun(2, "--gpus", "2", "--steps", "3", "--warmup", "3", "--seqs", "512,4096", "--lc-seq", "16384")
+    assert out["n_gpus"] == 2 and out["value"] > 0 and out["scaling"] == "strong", out
+    assert out["config"]["batch_per_gpu"] == 16 and out["config"]["global_batch"] == 32, out
+    assert out["pipeline_status"] == {"headline_and_e2e": 0, "after_sweep_and_long_context": 0}, out
+    assert out["e2e"]["outputs_match"] and len(out["e2e"]["h2d_gbs_per_rank"]) == 2, out
+    assert len(out["sweep"]["points"]) == 4, out
+    assert out["long_context"]["vs_fp64_sampled_rows"]["within_tolerance"], out
 
 
 @needs2
