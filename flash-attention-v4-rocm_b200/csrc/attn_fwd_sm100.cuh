@@ -56,6 +56,7 @@ struct FwdParams {
   int num_mblocks;       // query blocks of QTILES*128 rows per (batch, head)
   int num_base_tiles;    // batch * heads * num_mblocks
   int num_tiles;         // num_base_tiles * splits
+  int num_items;         // paired causal schedule: work items (0 = plain stride over the tiles)
   const int* cu_q;        // packed sequences (Varlen): batch + 1 row offsets into Q / O (sq = total rows)
   const int* cu_k;        //   and into K / V (sk = total keys)
   uint32_t* status;
@@ -131,6 +132,34 @@ __device__ __forceinline__ int kv_tiles_for(const FwdParams& p, const TileCoord&
   return (hi - c.kv_begin + kBlockN - 1) / kBlockN;
 }
 
+// Work-tile schedules (the loops of all three roles walk the same one).
+//
+// Plain: tiles blockIdx.x, blockIdx.x + gridDim.x, ... of the order tile_coord
+// defines. Paired (the Paired instantiation, causal without split or packed
+// sequences; the host picks it when it balances better): a work item is the
+// longest and the shortest query block of one (batch, head) -- m-blocks
+// nm-1-q and q -- run back to back by one CTA, so every item has the same
+// number of K/V steps (a middle block without a partner runs alone) and both
+// tiles read the same head's K/V. Items go batch by batch, pairs outermost,
+// heads interleaved, and CTAs take them with a stride of gridDim.x. A CTA's
+// paired tiles are listed once in shared memory at kernel start
+// (build_pair_list); the host keeps the list within kMaxListTiles.
+constexpr int kMaxListTiles = 127;  // + their count: 512 bytes
+
+// This CTA's paired tiles in tile_coord's causal order (w = (nm - 1 -
+// m-block) * heads + head); returns how many.
+__device__ __forceinline__ int build_pair_list(const FwdParams& p, int* list) {
+  const int nm = p.num_mblocks, per_b = ((nm + 1) >> 1) * p.heads;
+  int n = 0;
+  for (int item = blockIdx.x; item < p.num_items && n + 2 <= kMaxListTiles; item += gridDim.x) {
+    const int b = item / per_b, r = item - b * per_b;
+    const int q = r / p.heads, h = r - q * p.heads;
+    list[n++] = b * p.heads * nm + r;  // the long tile: m-block nm - 1 - q, w = q * heads + h = r
+    if (nm - 1 - q != q) list[n++] = b * p.heads * nm + (nm - 1 - q) * p.heads + h;
+  }
+  return n;
+}
+
 // Shared memory: Q tiles, then a ring of 64 KiB slots, then barriers. Per work
 // tile the load warp fills the ring with the groups G(-1) = {K0},
 // G(j) = {V_j, K_j+1} (j = 0..N-2) and G(N-1) = {V_N-1}: exactly what the MMA
@@ -149,7 +178,8 @@ struct SmemLayout {
   static constexpr int kTeardown = kNumBars - 1;
   static constexpr int kTmemHolder = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemHolder + 4;
-  static constexpr int kStage = (kAbort + 4 + 1023) & ~1023;  // [Q tile] O store stage: 128 rows x 128 B
+  static constexpr int kList = (kAbort + 4 + 15) & ~15;         // paired schedule: this CTA's tiles
+  static constexpr int kStage = (kList + 4 * (kMaxListTiles + 1) + 1023) & ~1023;  // [Q tile] O store stage: 128 rows x 128 B
   static constexpr int kBytes = kStage + QTiles * kBoxBytes;
   static constexpr int kAlloc = kBytes + 1024;                // slack for 1 KiB alignment
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
@@ -253,7 +283,7 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[128], float sca
 }
 
 // ---------------------------------------------------------------------------
-template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split, bool Varlen>
+template <bool Causal, int QTiles, int Slots, int PolyPer8, bool Split, bool Varlen, bool Paired = false>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -266,6 +296,7 @@ __global__ void __launch_bounds__(384, 1)
   auto bar = [&](int slot) -> uint32_t { return bar0 + 8u * slot; };
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kAbort);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kTmemHolder);
+  int* tile_list = reinterpret_cast<int*>(smem + L::kList);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -287,6 +318,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     mbar_init(bar(L::kTeardown), 1);
     fence_mbar_init();
+    if (Paired) tile_list[kMaxListTiles] = build_pair_list(p, tile_list);
   }
   if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&tm_q);
@@ -302,12 +334,14 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  const int list_len = Paired ? tile_list[kMaxListTiles] : 0;  // paired schedule: this CTA's tiles
 
   // 384 threads launched with kLaunchRegs registers each (ptxas must report
   // exactly that: __launch_bounds__(384, 1) caps it at 168). Softmax
   // warpgroups take kSoftmaxRegs, the load/MMA warpgroup keeps kOtherRegs:
   // 128 * (2 * 216 + 72) = 64512 = 384 * 168.
   static_assert(128 * (2 * kSoftmaxRegs + kOtherRegs) <= 384 * kLaunchRegs, "register split exceeds the launch");
+  static_assert(!Paired || (Causal && !Split && !Varlen), "the paired schedule is for causal tiles of one launch");
 
   if (warp >= 8) {
     regs_release<kOtherRegs>();
@@ -321,7 +355,8 @@ __global__ void __launch_bounds__(384, 1)
       // parity each stage was last armed with, for the drain on abort
       uint32_t armed_mask = 0, armed_par = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int v = Paired ? 0 : blockIdx.x; v < (Paired ? list_len : p.num_tiles) && ok; v += Paired ? 1 : gridDim.x) {
+        const int t = Paired ? tile_list[v] : v;
         const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
@@ -411,7 +446,8 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
       };
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int v = Paired ? 0 : blockIdx.x; v < (Paired ? list_len : p.num_tiles) && ok; v += Paired ? 1 : gridDim.x) {
+        const int t = Paired ? tile_list[v] : v;
         const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
         const int n0 = kv_tiles_for<Causal>(p, tc, tc.m0);
         const int n1 = QTiles > 1 ? kv_tiles_for<Causal>(p, tc, tc.m0 + kBlockM) : 0;
@@ -487,7 +523,8 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t s_par = 0, o_full_par = 0;
     const float scale_log2 = p.scale_log2;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    for (int v = Paired ? 0 : blockIdx.x; v < (Paired ? list_len : p.num_tiles) && ok; v += Paired ? 1 : gridDim.x) {
+      const int t = Paired ? tile_list[v] : v;
       const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
       const int r0 = tc.m0 + i * kBlockM;
       const int ni = kv_tiles_for<Causal>(p, tc, r0);

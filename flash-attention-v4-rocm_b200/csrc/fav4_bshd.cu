@@ -84,6 +84,70 @@ bool args_valid(const Fav4Args* a, int causal, int config) {
   return true;
 }
 
+// Causal work-tile schedule (see sched_tile in attn_fwd_sm100.cuh): the number
+// of head-pair work items when pairing gives the shorter estimated makespan
+// on `sms` persistent CTAs, else 0 (plain stride). A tile costs its K/V steps
+// plus one for its fill and drain. Both schedules are simulated (tile costs
+// depend only on the query block); decisions are cached per shape.
+int paired_items(int batch, int heads, int sq, int sk, int qtiles, int sms) {
+  const int rows = qtiles * kBlockM;
+  const int nm = (sq + rows - 1) / rows;
+  const int64_t tiles = static_cast<int64_t>(batch) * heads * nm;
+  const int64_t items = static_cast<int64_t>(batch) * heads * ((nm + 1) / 2);
+  if (nm < 2 || items > INT_MAX || sms <= 0) return 0;
+  struct Entry {
+    int batch, heads, sq, sk, qtiles, sms, items;
+  };
+  constexpr int kCache = 32;
+  static std::mutex mu;
+  static Entry cache[kCache];
+  static int used = 0, next = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int e = 0; e < used; ++e) {
+      const Entry& c = cache[e];
+      if (c.batch == batch && c.heads == heads && c.sq == sq && c.sk == sk && c.qtiles == qtiles && c.sms == sms)
+        return c.items;
+    }
+  }
+  auto cost = [&](int mb) -> int64_t {  // K/V steps of the work tile at query block mb, + 1
+    int n = 0;
+    for (int i = 0; i < qtiles; ++i) {
+      const int r0 = mb * rows + i * kBlockM;
+      if (r0 >= sq) continue;
+      const int hi = r0 + kBlockM < sk ? r0 + kBlockM : sk;
+      const int ni = (hi + kBlockN - 1) / kBlockN;
+      n = ni > n ? ni : n;
+    }
+    return n > 0 ? n + 1 : 0;
+  };
+  constexpr int kMaxGrid = 1024;
+  int64_t load[kMaxGrid];
+  // plain stride: tile t has query block nm - 1 - (t % (heads * nm)) / heads
+  const int g1 = static_cast<int>(tiles < sms ? tiles : sms);
+  const int g2 = static_cast<int>(items < sms ? items : sms);
+  if (g1 > kMaxGrid || g2 > kMaxGrid) return 0;
+  int64_t span_stride = 0, span_pairs = 0;
+  for (int c = 0; c < g1; ++c) load[c] = 0;
+  for (int64_t t = 0; t < tiles; ++t) load[t % g1] += cost(nm - 1 - static_cast<int>(t % (heads * nm)) / heads);
+  for (int c = 0; c < g1; ++c) span_stride = load[c] > span_stride ? load[c] : span_stride;
+  for (int c = 0; c < g2; ++c) load[c] = 0;
+  const int per_b = ((nm + 1) / 2) * heads;
+  for (int64_t it = 0; it < items; ++it) {
+    const int q = static_cast<int>(it % per_b) / heads;
+    load[it % g2] += cost(nm - 1 - q) + (nm - 1 - q != q ? cost(q) : 0);
+  }
+  for (int c = 0; c < g2; ++c) span_pairs = load[c] > span_pairs ? load[c] : span_pairs;
+  // a CTA lists at most kMaxListTiles paired tiles (two per item)
+  const bool fits = 2 * ((items + g2 - 1) / g2) <= kMaxListTiles;
+  const int result = (fits && span_pairs < span_stride) ? static_cast<int>(items) : 0;
+  std::lock_guard<std::mutex> lock(mu);
+  cache[next] = Entry{batch, heads, sq, sk, qtiles, sms, result};
+  next = (next + 1) % kCache;
+  used = used < kCache ? used + 1 : used;
+  return result;
+}
+
 // B200 tilings behind the reference's config ids (include/fav4_bshd.h:17-18):
 //   1: one 128-row Q tile per CTA, 2 K/V ring slots, MUFU exp2 only
 //   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
@@ -100,15 +164,25 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int sp
   if (e != cudaSuccess) return e;
   DeviceInfo info;
   if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
-  auto kernel = attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split, Varlen>;
   constexpr int smem = SmemLayout<QTiles, Slots>::kAlloc;
+  constexpr bool kPairable = Causal && !Split && !Varlen;
+  const int items = kPairable ? paired_items(a.batch, a.heads, a.sq, a.sk, QTiles, info.sms) : 0;
+  // [0]: plain schedule, [1]: paired schedule (the same kernel where it does not apply)
+  decltype(&attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split, Varlen, false>) variants[2] = {
+      attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split, Varlen, false>,
+      attn_fwd_sm100_kernel<Causal, QTiles, Slots, PolyPer8, Split, Varlen, kPairable>};
+  auto kernel = variants[items > 0 ? 1 : 0];
   {
+    // both variants get their attribute on the first call, so later calls set
+    // nothing whichever schedule they pick
     static std::mutex mu;
     static bool attr_set[kMaxDevices] = {};
     std::lock_guard<std::mutex> lock(mu);
     if (!attr_set[dev]) {
-      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
+      for (auto fn : variants) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+      }
       attr_set[dev] = true;
     }
   }
@@ -139,9 +213,11 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int sp
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
   p.num_base_tiles = static_cast<int>(base);
   p.num_tiles = static_cast<int>(tiles);
+  p.num_items = items;
   p.status = info.status;
   p.wait_limit_ns = wait_limit_ns();
-  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  const int64_t work = p.num_items > 0 ? p.num_items : tiles;
+  const int grid = static_cast<int>(work < info.sms ? work : info.sms);
   kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }

@@ -139,3 +139,25 @@ def test_varlen_against_oracle(runner, cuda, causal, h, hk):
         R.errors(got_o, got_l, ref, ref_lse)
     assert math.isfinite(float(o.float().sum()))
     assert runner.pipeline_status() == 0
+
+
+@pytest.mark.parametrize("b,s,h", [(4, 4096, 8), (2, 4096, 8), (16, 4096, 8), (3, 2944, 5), (1, 16384, 8)])
+def test_causal_schedules_agree(runner, cuda, b, s, h):
+    """Causal launches of one batch of equal sequences pick the head-pair
+    schedule when it balances better (the host simulates both); packed
+    sequences always take the plain one. Every tile computes the same numbers
+    either way, so the two outputs agree bit for bit, and both cover every row
+    (NaN pre-fill)."""
+    q, k, v = _inputs((b, s, h, 128), 11)
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((b, h, s), float("nan"), device="cuda")
+    runner.call(q, k, v, o, lse, True, 0)
+    cu = torch.arange(0, (b + 1) * s, s, device="cuda", dtype=torch.int32)
+    ov = torch.full((b * s, h, 128), float("nan"), device="cuda", dtype=torch.bfloat16)
+    lv = torch.full((h, b * s), float("nan"), device="cuda")
+    runner.call_varlen(q.view(b * s, h, 128), k.view(b * s, h, 128), v.view(b * s, h, 128), ov, lv, cu, cu, s,
+                       True, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(o.view(b * s, h, 128), ov)
+    assert torch.equal(lse.permute(1, 0, 2).reshape(h, b * s), lv)
+    assert runner.pipeline_status() == 0
