@@ -11,7 +11,10 @@ length before timing it (benchmarks/bshd.py:147-156, R.sample_rows):
   (fav4_bshd.splitkv): zigzag key chunks per "rank", each rank's two chunk
   partials merged, then the ranks' partials combined -- all on one device;
 * packed variable-length sequences (fav4_bshd_forward_varlen) checked directly
-  against the oracle, sequence by sequence, grouped-query heads included.
+  against the oracle, sequence by sequence, grouped-query heads included;
+* the causal work-tile schedules: a batch the host runs with head-pair work
+  items against the same rows as packed sequences (plain schedule), bit for
+  bit.
 """
 import functools
 import math
