@@ -665,24 +665,27 @@ __global__ void __launch_bounds__(384, 1)
         // The ragged last Q tile of a packed sequence is stored row by row: a 128-row TMA box would
         // also write the next sequence's rows. Tile-uniform, so all four warps take the same path.
         const bool direct = Varlen && r0 + kBlockM > tc.sq;
+        // All 128 columns of the O row in one batch of TMEM loads and one wait:
+        // loads issued one by one each wait behind the other tile's MMAs.
+        // O_i is free for the next work tile as soon as it is in registers.
+        uint32_t oall[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_o + c * 32, oall[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();  // every lane has read its row of O_i
+        if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            uint32_t orow[32];
-            tmem_ld32(t_o + half * 64 + c * 32, orow);
-            tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-              pk[c * 16 + e] = pack_bf16x2(__uint_as_float(orow[2 * e]) * inv, __uint_as_float(orow[2 * e + 1]) * inv);
+              pk[c * 16 + e] = pack_bf16x2(__uint_as_float(oall[half * 2 + c][2 * e]) * inv,
+                                           __uint_as_float(oall[half * 2 + c][2 * e + 1]) * inv);
           }
-          if (half == 1) {
-            tc_fence_before();
-            __syncwarp();  // every lane has read its row of O_i
-            if (lane == 0) mbar_arrive(bar(L::kOEmpty + i));
-            if (!direct) pair_all(1 + i, 128, true);  // the store of columns 0-63 has read the stage
-          }
+          if (half == 1 && !direct) pair_all(1 + i, 128, true);  // the store of columns 0-63 has read the stage
           if (direct) {
             if (live) {
               uint4* dst = reinterpret_cast<uint4*>(p.o + orow * kHeadDim + half * 64);
