@@ -393,6 +393,11 @@ __global__ void __launch_bounds__(384, 1)
   // 128 * (2 * 216 + 72) = 64512 = 384 * 168.
   static_assert(128 * (2 * kSoftmaxRegs + kOtherRegs) <= 384 * kLaunchRegs, "register split exceeds the launch");
   static_assert(!Paired || (Causal && !Split && !Varlen), "the paired schedule is for causal tiles of one launch");
+  // One Q tile per CTA (config 1): S is double-buffered in TMEM (the second Q
+  // tile's columns are free), so S is computed two K/V steps ahead of PV and
+  // the softmax of step j overlaps the MMAs of steps j-1 and j+1. Two Q tiles:
+  // one S buffer per tile, the tiles ping-pong, S one step ahead.
+  constexpr int KA = QTiles == 1 ? 2 : 1;
 
   if (warp >= 8) {
     regs_release<kOtherRegs>();
@@ -422,12 +427,15 @@ __global__ void __launch_bounds__(384, 1)
           tma_load_4d(dst, &tm_q, bar(L::kQFull), 0, tc.h, tc.q0 + tc.m0 + i * kBlockM, tc.tb, pol_q);
           tma_load_4d(dst + kBoxBytes, &tm_q, bar(L::kQFull), 64, tc.h, tc.q0 + tc.m0 + i * kBlockM, tc.tb, pol_q);
         }
-        for (int g = -1; g < N && ok; ++g) {
+        // Groups G(g) = {V_g, K_(g+KA)} for g = -KA .. N-1 (empty ones skipped):
+        // the MMA thread computes S KA steps ahead of PV (see the MMA issuer).
+        for (int g = -KA; g < N && ok; ++g) {
+          const bool has_v = g >= 0, has_k = g + KA < N;
+          if (KA > 1 && !has_v && !has_k) continue;
           if (!mbar_wait(bar(L::kKVEmpty + ring.stage), ring.phase ^ 1u, ctl, kStatusTimeoutLoad)) {
             ok = false;
             break;
           }
-          const bool has_v = g >= 0, has_k = g + 1 < N;
           const uint32_t fb = bar(L::kKVFull + ring.stage);
           mbar_arrive_expect_tx(fb, (has_v ? kTileBytes : 0) + (has_k ? kTileBytes : 0));
           st.arm(ring.stage, ring.phase);
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(384, 1)
             tma_load_4d(dst + kBoxBytes, &tm_v, fb, 64, kvh, sv, tc.tb, pol_kv);
           }
           if (has_k) {
-            const int sk0 = tc.k0 + tc.kv_begin + (g + 1) * kBlockN;
+            const int sk0 = tc.k0 + tc.kv_begin + (g + KA) * kBlockN;
             tma_load_4d(dst + kTileBytes, &tm_k, fb, 0, kvh, sk0, tc.tb, pol_kv);
             tma_load_4d(dst + kTileBytes + kBoxBytes, &tm_k, fb, 64, kvh, sk0, tc.tb, pol_kv);
           }
@@ -494,6 +502,26 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
       };
+      // One Q tile (QTiles == 1): S buffer b at TMEM columns 128 b, O at 256.
+      auto issue_s_buf = [&](int b, int slot) {
+        const uint32_t qa = k_lo + (L::kQ >> 4);
+        const uint32_t ka = k_lo + ((L::kKV + slot * L::kSlotBytes + kTileBytes) >> 4);
+        const uint32_t d = tmem + b * 128;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k) {
+          const uint32_t off = ((k / 4) * kBoxBytes + (k % 4) * 32) >> 4;
+          umma_ss_w(d, qa + off, k_hi, ka + off, k_hi, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(L::kSFull + b));
+      };
+      auto issue_pv_buf = [&](int b, int slot, bool acc) {
+        const uint32_t va = v_lo + ((L::kKV + slot * L::kSlotBytes) >> 4);
+        const uint32_t d = tmem + 256;
+        const uint32_t pa = tmem + b * 128;
+        umma_ts_w(d, pa, va, v_hi, idesc_pv, acc ? 1u : 0u);
+#pragma unroll
+        for (int k = 1; k < kBlockN / 16; ++k) umma_ts_w(d, pa + k * 8, va + ((k * 2048) >> 4), v_hi, idesc_pv, 1u);
+      };
       for (int v = Paired ? 0 : blockIdx.x; v < (Paired ? list_len : p.num_tiles) && ok; v += Paired ? 1 : gridDim.x) {
         const int t = Paired ? tile_list[v] : v;
         const TileCoord tc = tile_coord<Causal, QTiles, Split, Varlen>(p, t);
@@ -503,6 +531,48 @@ __global__ void __launch_bounds__(384, 1)
         if (N == 0) continue;
         if (!mbar_wait(bar(L::kQFull), par.q_full(), ctl, kStatusTimeoutMma)) { ok = false; break; }
         par.flip_q_full();
+        if constexpr (QTiles == 1) {
+          // S buffer b = j % 2 (TMEM columns 128 b). Prologue: S(0) from G(-2) = {K0}
+          // and S(1) from G(-1) = {K1}; step j: PV(j) from buffer j % 2, then S(j+2)
+          // into the same buffer (after PV(j) has read P(j), in issue order), both
+          // from G(j) = {V_j, K_j+2}. Every PV is committed to pv_done (the o_full
+          // barrier of the unused second tile) so the softmax can wait for PV(j-1)
+          // before it rescales O.
+          for (int pb = 0; pb < 2 && pb < N && ok; ++pb) {
+            if (!mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_s_buf(pb, ring.stage);
+            tc_commit(bar(L::kKVEmpty + ring.stage));
+            ring.advance<Slots>();
+          }
+          if (N <= 2 && ok) tc_commit(bar(L::kQEmpty));
+          if (ok && !mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) ok = false;
+          for (int j = 0; j < N && ok; ++j) {
+            const int b = j & 1;
+            const int cur = ring.stage;
+            Ring nxt = ring;
+            nxt.advance<Slots>();
+            if (!mbar_wait(bar(L::kPFull + b), par.p_full(b), ctl, kStatusTimeoutMma)) { ok = false; break; }
+            par.flip_p_full(b);
+            if (j == 0) {
+              if (!mbar_wait(bar(L::kOEmpty), par.o_empty(0), ctl, kStatusTimeoutMma)) { ok = false; break; }
+              par.flip_o_empty(0);
+            }
+            tc_fence_after();
+            issue_pv_buf(b, cur, j > 0);
+            tc_commit(bar(L::kOFull + 1));  // pv_done
+            if (j + 1 == N) tc_commit(bar(L::kOFull));
+            if (j + 2 < N) issue_s_buf(b, cur);
+            tc_commit(bar(L::kKVEmpty + cur));  // V_j and K_j+2 are no longer read
+            if (j + 3 == N) tc_commit(bar(L::kQEmpty));
+            ring = nxt;
+            if (j + 1 < N && !mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+          }
+          continue;
+        }
         // group G(-1) = {K0}
         if (!mbar_wait(bar(L::kKVFull + ring.stage), ring.phase, ctl, kStatusTimeoutMma)) { ok = false; break; }
         tc_fence_after();
@@ -562,13 +632,14 @@ __global__ void __launch_bounds__(384, 1)
     const int i = warp / 4;                  // Q tile served by this warpgroup
     const int row = (warp % 4) * 32 + lane;  // TMEM lane = row within the Q tile
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + i * 128;
+    const uint32_t t_s0 = tmem + lane_off + i * 128;  // one Q tile: S buffer j % 2 at t_s0 + 128 (j % 2)
     const uint32_t t_o = tmem + lane_off + 256 + i * 128;
     // O store stage of this Q tile: 16-byte chunk c of a row at (c ^ (row % 8)), the TMA 128-byte swizzle
     uint8_t* stage_row = smem + L::kStage + i * kBoxBytes + row * 128;
     const uint32_t stage = sbase + L::kStage + i * kBoxBytes;
     const bool issuer = warp % 4 == 0 && lane == 0;  // issues this warpgroup's O stores
-    uint32_t s_par = 0, o_full_par = 0;
+    uint32_t s_par = 0, o_full_par = 0;  // one Q tile: s_par bit b for S buffer b
+    uint32_t pv_seen = 0;                 // one Q tile: PVs of earlier work tiles (pv_done phases)
     const float scale_log2 = p.scale_log2;
     bool ok = true;
     for (int v = Paired ? 0 : blockIdx.x; v < (Paired ? list_len : p.num_tiles) && ok; v += Paired ? 1 : gridDim.x) {
@@ -582,8 +653,11 @@ __global__ void __launch_bounds__(384, 1)
         if (r0 >= tc.sq) continue;  // padding-only Q tile: nothing to write
       }
       for (int j = 0; j < ni; ++j) {
-        if (!warp_wait(bar(L::kSFull + i), s_par, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
-        s_par ^= 1u;
+        const int sb = QTiles == 1 ? (j & 1) : i;  // S buffer / barrier of this step
+        const uint32_t t_s = t_s0 + (QTiles == 1 ? sb * 128 : 0);
+        const uint32_t s_bit = QTiles == 1 ? 1u << sb : 1u;
+        if (!warp_wait(bar(L::kSFull + sb), (s_par & s_bit) ? 1u : 0u, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+        s_par ^= s_bit;
         tc_fence_after();
         uint32_t sr[4][32];
 #pragma unroll
@@ -625,9 +699,16 @@ __global__ void __launch_bounds__(384, 1)
                                     : exp_pack_store<PolyPer8, false>(s, scale_log2, mb, t_s);
         l = l * alpha + rowsum;
         if (rescale) {
-          // Lazy correction: O_i already holds P V of the previous tiles (the
-          // S commit that released this tile covers that PV); the row owner
-          // rescales it in TMEM before PV of this tile is issued.
+          // Lazy correction: the row owner rescales O_i in TMEM before PV of
+          // this tile is issued. O_i must hold P V of all previous tiles: with
+          // two Q tiles the S commit that released this tile covers PV(j-1);
+          // with one (S two steps ahead) it covers only PV(j-2), so wait for
+          // pv_done's completion of PV(j-1) (phases count every PV of the CTA).
+          if (QTiles == 1) {
+            const uint32_t ph = (pv_seen + j - 1) & 1u;
+            if (!warp_wait(bar(L::kOFull + 1), ph, ctl, kStatusTimeoutSoftmax)) { ok = false; break; }
+            tc_fence_after();
+          }
           const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -646,8 +727,9 @@ __global__ void __launch_bounds__(384, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();  // every lane's P / O stores are complete
-        if (lane == 0) mbar_arrive(bar(L::kPFull + i));
+        if (lane == 0) mbar_arrive(bar(L::kPFull + sb));
       }
+      pv_seen += ni;
       // ------------------------------ epilogue ------------------------------
       const bool live = grow < tc.sq;
       // O row of this thread: [ob][q0 + grow] in a tensor of sq rows per batch entry
