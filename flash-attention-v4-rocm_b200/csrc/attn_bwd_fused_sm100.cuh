@@ -61,6 +61,8 @@ struct BwdFusedParams {
   float scale, scale_log2;
   int num_outer;      // key tiles per (batch, head)
   int num_tiles;      // batch * kv_heads * num_outer
+  int num_items;      // causal head-pair schedule: work items (0 = plain stride over the tiles)
+  int num_slots;      // loop positions the CTAs stride over (num_tiles, or 2 gridDim.x ceil(items / gridDim.x))
   uint32_t* status;
   uint64_t wait_limit_ns;
 };
@@ -117,6 +119,29 @@ __device__ __forceinline__ BwdSeq bwd_seq(const BwdFusedParams& p, int b) {
   const int qa = min(max(__ldg(p.cu_q + b), 0), p.sq), qe = min(max(__ldg(p.cu_q + b + 1), qa), p.sq);
   const int ka = min(max(__ldg(p.cu_k + b), 0), p.sk), ke = min(max(__ldg(p.cu_k + b + 1), ka), p.sk);
   return BwdSeq{qa, min(qe - qa, p.max_sq), ka, min(ke - ka, p.max_sk)};
+}
+
+// Work tile at loop position v; every role walks v = blockIdx.x, + gridDim.x, ...
+// below p.num_slots. Plain schedule: tile v of bwd_tile's order. Head-pair
+// schedule (causal, p.num_items > 0; the host picks it when it balances
+// better): a work item is the key tile q with the most query tiles to walk and
+// the key tile nk-1-q with the fewest, of one (batch, K/V head), so all items
+// cost the same and both read the same head's Q and dO. The long tile runs at
+// position (2 (item / G)) G + item % G and the short one a wave later, on the
+// same CTA (G = gridDim.x). -1: an empty position (past the last item, or the
+// missing partner of a middle key tile).
+__device__ __forceinline__ int bwd_sched(const BwdFusedParams& p, int v) {
+  if (p.num_items == 0) return v;
+  const int g = gridDim.x;
+  const int w = v / g;
+  const int item = (w >> 1) * g + (v - w * g);
+  if (item >= p.num_items) return -1;
+  const int nk = p.num_outer, per_b = ((nk + 1) >> 1) * p.kv_heads;
+  const int b = item / per_b, r = item - b * per_b;
+  const int q = r / p.kv_heads, h = r - q * p.kv_heads;
+  if ((w & 1) && nk - 1 - q == q) return -1;
+  const int k = (w & 1) ? nk - 1 - q : q;
+  return (b * nk + k) * p.kv_heads + h;  // bwd_tile: w = k * kv_heads + h within batch entry b
 }
 
 template <bool Causal, bool Varlen>
@@ -191,7 +216,9 @@ __global__ void __launch_bounds__(512, 1)
       uint32_t kv_empty_par = 1;
       uint32_t armed = 0, armed_par = 0;  // stages (bits 0-1) and the K/V pair (bit 2) in flight
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int v = blockIdx.x; v < p.num_slots && ok; v += gridDim.x) {
+      const int t = bwd_sched(p, v);
+      if (t < 0) continue;
         int b, h, idx, lo, hi;
         bwd_tile<Causal>(rp, t, b, h, idx, true);
         const int o0 = idx * kBlockN;
@@ -291,7 +318,9 @@ __global__ void __launch_bounds__(512, 1)
           umma_ss_w(tmem + 128, v_lo + ((L::kDS + k * 2048) >> 4), v_hi, v_lo + ((L::kK + k * 2048) >> 4), v_hi,
                     idesc_dq, k > 0 ? 1u : 0u);
       };
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int v = blockIdx.x; v < p.num_slots && ok; v += gridDim.x) {
+      const int t = bwd_sched(p, v);
+      if (t < 0) continue;
         int b, h, idx, lo, hi;
         bwd_tile<Causal>(rp, t, b, h, idx, true);
         const BwdSeq sq = bwd_seq<Varlen>(p, b);
@@ -366,7 +395,9 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
     uint32_t dq_par = 0, acc_full_par = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    for (int v = blockIdx.x; v < p.num_slots && ok; v += gridDim.x) {
+      const int t = bwd_sched(p, v);
+      if (t < 0) continue;
       int b, h, idx, lo, hi;
       bwd_tile<Causal>(rp, t, b, h, idx, true);
       const int o0 = idx * kBlockN;
@@ -465,7 +496,9 @@ __global__ void __launch_bounds__(512, 1)
     uint32_t s_par = 0, dp_par = 0;
     bool ok = true;
     const float2 sc = make_float2(p.scale_log2, p.scale_log2);
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    for (int v = blockIdx.x; v < p.num_slots && ok; v += gridDim.x) {
+      const int t = bwd_sched(p, v);
+      if (t < 0) continue;
       int b, h, idx, lo, hi;
       bwd_tile<Causal>(rp, t, b, h, idx, true);
       const int o0 = idx * kBlockN;

@@ -745,6 +745,39 @@ int launch_bwd(const BwdParams& base, const CUtensorMap& o0, const CUtensorMap& 
   return cudaGetLastError();
 }
 
+// Causal backward schedule (see bwd_sched in attn_bwd_fused_sm100.cuh): the
+// number of head-pair work items when pairing gives the shorter estimated
+// makespan on `sms` CTAs, else 0. A key tile k walks the query tiles k..nq-1
+// of each query head of its group; it costs those steps plus one.
+int bwd_paired_items(int batch, int kv_heads, int group, int sq, int sk, int sms) {
+  const int nq = (sq + kBlockM - 1) / kBlockM, nk = (sk + kBlockN - 1) / kBlockN;
+  const int64_t tiles = static_cast<int64_t>(batch) * kv_heads * nk;
+  const int64_t items = static_cast<int64_t>(batch) * kv_heads * ((nk + 1) / 2);
+  if (nk < 2 || items > INT_MAX / 2 || sms <= 0) return 0;
+  auto cost = [&](int k) -> int64_t {
+    const int o0 = k * kBlockN;
+    if (o0 >= sk || o0 >= sq) return 1;
+    return static_cast<int64_t>(nq - o0 / kBlockM) * group + 1;
+  };
+  constexpr int kMaxGrid = 1024;
+  int64_t load[kMaxGrid];
+  const int g1 = static_cast<int>(tiles < sms ? tiles : sms);
+  const int g2 = static_cast<int>(items < sms ? items : sms);
+  if (g1 > kMaxGrid || g2 > kMaxGrid || tiles > (int64_t(1) << 22)) return 0;
+  int64_t span_stride = 0, span_pairs = 0;
+  for (int c = 0; c < g1; ++c) load[c] = 0;
+  for (int64_t t = 0; t < tiles; ++t) load[t % g1] += cost(static_cast<int>(t % (int64_t(kv_heads) * nk)) / kv_heads);
+  for (int c = 0; c < g1; ++c) span_stride = load[c] > span_stride ? load[c] : span_stride;
+  for (int c = 0; c < g2; ++c) load[c] = 0;
+  const int per_b = ((nk + 1) / 2) * kv_heads;
+  for (int64_t it = 0; it < items; ++it) {
+    const int q = static_cast<int>(it % per_b) / kv_heads;
+    load[it % g2] += cost(q) + (nk - 1 - q != q ? cost(nk - 1 - q) : 0);
+  }
+  for (int c = 0; c < g2; ++c) span_pairs = load[c] > span_pairs ? load[c] : span_pairs;
+  return span_pairs < span_stride ? static_cast<int>(items) : 0;
+}
+
 template <bool Causal, bool Varlen>
 int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& tq, const CUtensorMap& tdo, const DeviceInfo& info, int dev,
@@ -766,7 +799,10 @@ int launch_bwd_fused(const BwdFusedParams& base, const CUtensorMap& tk, const CU
   const int64_t tiles = static_cast<int64_t>(p.batch) * p.kv_heads * p.num_outer;
   if (tiles > INT_MAX) return cudaErrorInvalidValue;
   p.num_tiles = static_cast<int>(tiles);
-  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  p.num_items = (Causal && !Varlen) ? bwd_paired_items(p.batch, p.kv_heads, p.group, p.sq, p.sk, info.sms) : 0;
+  const int64_t work = p.num_items > 0 ? p.num_items : tiles;
+  const int grid = static_cast<int>(work < info.sms ? work : info.sms);
+  p.num_slots = p.num_items > 0 ? 2 * grid * ((p.num_items + grid - 1) / grid) : p.num_tiles;
   kernel<<<grid, 512, smem, stream>>>(tk, tv, tq, tdo, p);
   return cudaGetLastError();
 }

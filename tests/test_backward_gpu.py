@@ -180,3 +180,22 @@ def test_backward_peaky_softmax(runner, causal, deterministic):
     for g, w, n in zip(got, want, ("dq", "dk", "dv")):
         _check(g, w, n)
     assert runner.pipeline_status() == 0
+
+
+@pytest.mark.parametrize("b,h,hk,s", [(4, 8, 8, 4096), (2, 8, 2, 4096), (1, 8, 8, 16384)])
+def test_causal_head_pair_schedule(runner, b, h, hk, s):
+    """Causal shapes large enough for the host to run the fused backward with
+    head-pair work items (a head's longest and shortest key tile on one CTA):
+    dK and dV equal the deterministic path's bit for bit (which walks its key
+    tiles with the plain schedule), and dQ agrees with it within the FP32
+    reduction-order tolerance of test_fused_dk_dv_match_deterministic_bitwise."""
+    q, k, v, do = _inputs(b, h, s, s, 41)
+    if hk != h:
+        k, v = k[:, :, :hk].contiguous(), v[:, :, :hk].contiguous()
+    scale = 1 / math.sqrt(128)
+    fused = _run(runner, q, k, v, do, True, scale)
+    det = _run(runner, q, k, v, do, True, scale, deterministic=True)
+    assert torch.equal(fused[1], det[1]) and torch.equal(fused[2], det[2])
+    err = (fused[0].float() - det[0].float()).abs().max().item()
+    assert err <= 0.01 * det[0].float().abs().max().item() + 1e-3, err
+    assert runner.pipeline_status() == 0
