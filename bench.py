@@ -443,9 +443,12 @@ def run_backward(args):
 def run_decode(args):
     """Decode-like shapes on one GPU (few query rows against a long key cache):
     fav4_bshd_forward against the one-launch split-KV forward with the
-    automatic split count, on the same tensors. One JSON line per shape with
-    both times, the split count, and the K/V bytes read per microsecond (the
-    path is HBM-bound: every key and value is read once)."""
+    automatic split count, on the same tensors. Both are timed as K calls
+    replayed from a CUDA graph (device time: at tens of microseconds per call
+    the host's per-call work would otherwise be measured); the split path is
+    also timed launched call by call. One JSON line per shape with the times,
+    the split count, and the K/V bytes read per microsecond (the path is
+    HBM-bound: every key and value is read once)."""
     import torch
 
     import fav4_bshd
@@ -464,23 +467,38 @@ def run_decode(args):
             torch.cuda.synchronize()
             diff = float((o.float() - o_split.float()).abs().max())
 
-            def timed(fn):
+            def timed(fn, graph):
                 for _ in range(max(3, args.warmup)):
                     fn()
                 torch.cuda.synchronize()
+                if graph:  # device time: the calls replayed from a CUDA graph (no host work per call)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        for _ in range(args.steps):
+                            fn()
+                    g.replay()
+                    torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                for _ in range(args.steps):
-                    fn()
+                if graph:
+                    g.replay()
+                else:
+                    for _ in range(args.steps):
+                        fn()
                 e1.record()
                 torch.cuda.synchronize()
                 return e0.elapsed_time(e1) * 1e3 / args.steps
 
-            us_plain = timed(lambda: runner.call(q, k, v, o, None, False, args.config))
-            us_split = timed(lambda: runner.call_splitkv(q, k, v, o_split, None, False, args.config, used))
+            plain = lambda: runner.call(q, k, v, o, None, False, args.config)  # noqa: E731
+            split = lambda: runner.call_splitkv(q, k, v, o_split, None, False, args.config, used)  # noqa: E731
+            us_plain, us_split = timed(plain, True), timed(split, True)
+            us_split_eager = timed(split, False)
             kv_bytes = 2 * b * sk * h * D * 2
             emit({"mode": "decode", "batch": b, "heads": h, "sq": sq, "sk": sk, "splits": used,
                   "us_forward": us_plain, "us_splitkv": us_split, "speedup": us_plain / us_split,
+                  "us_splitkv_eager_calls": us_split_eager,
+                  "timing": f"{args.steps} calls replayed from one CUDA graph (device time); eager: the same "
+                            "calls launched one by one from Python",
                   "kv_gbs_splitkv": kv_bytes / us_split / 1e3,
                   "frac_of_measured_hbm": kv_bytes / us_split / 1e3 / pk["hbm_gbs"], "peak_source": pk_kind,
                   "max_abs_diff": diff, "config": args.config,
