@@ -9,15 +9,9 @@ import math
 import pytest
 import torch
 
+from grad_checks import dq_close
+
 pytestmark = pytest.mark.gpu
-
-
-def dq_close(got, want):
-    """dQ of the fused path against another run: FP32 reductions in a different order move a
-    BF16 value by at most one ulp (rtol 2^-7), and where partial sums cancel, by up to about
-    1e-5 of the gradient's largest magnitude (atol)."""
-    g, w = got.float(), want.float()
-    return torch.allclose(g, w, rtol=2 ** -7, atol=1e-4 * w.abs().max().item() + 1e-6)
 
 
 def _packed(lens_q, lens_k, h, hk, seed):
