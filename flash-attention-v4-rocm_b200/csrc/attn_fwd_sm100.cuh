@@ -42,6 +42,10 @@ constexpr float kRescaleThreshold = 8.0f;        // base-2 units, bshd_kernel.hp
 constexpr uint32_t kLaunchRegs = 168;            // 65536 / 384 rounded down to a multiple of 8
 constexpr uint32_t kSoftmaxRegs = 216;
 constexpr uint32_t kOtherRegs = 72;
+// One Q tile (warps 4-7 idle at kOtherRegs): the softmax warpgroup and the
+// load/MMA warpgroup take the freed registers, 128 * (232 + 72 + 136) <= 384 * 168.
+constexpr uint32_t kSoftmaxRegs1 = 232;
+constexpr uint32_t kOtherRegs1 = 136;
 
 struct FwdParams {
   __nv_bfloat16* o;
@@ -392,6 +396,7 @@ __global__ void __launch_bounds__(384, 1)
   // warpgroups take kSoftmaxRegs, the load/MMA warpgroup keeps kOtherRegs:
   // 128 * (2 * 216 + 72) = 64512 = 384 * 168.
   static_assert(128 * (2 * kSoftmaxRegs + kOtherRegs) <= 384 * kLaunchRegs, "register split exceeds the launch");
+  static_assert(128 * (kSoftmaxRegs1 + kOtherRegs + kOtherRegs1) <= 384 * kLaunchRegs, "one-tile split exceeds the launch");
   static_assert(!Paired || (Causal && !Split && !Varlen), "the paired schedule is for causal tiles of one launch");
   // One Q tile per CTA (config 1): S is double-buffered in TMEM (the second Q
   // tile's columns are free), so S is computed two K/V steps ahead of PV and
@@ -400,7 +405,7 @@ __global__ void __launch_bounds__(384, 1)
   constexpr int KA = QTiles == 1 ? 2 : 1;
 
   if (warp >= 8) {
-    regs_release<kOtherRegs>();
+    regs_release<(QTiles == 1 ? kOtherRegs1 : kOtherRegs)>();
     if (warp == 8) {
     // ============================ TMA producer ============================
     if (lane == 0) {
@@ -628,7 +633,7 @@ __global__ void __launch_bounds__(384, 1)
     }  // warps 10-11: idle
   } else if (warp < 4 * QTiles) {
     // ============================== softmax ===============================
-    regs_claim<kSoftmaxRegs>();
+    regs_claim<(QTiles == 1 ? kSoftmaxRegs1 : kSoftmaxRegs)>();
     const int i = warp / 4;                  // Q tile served by this warpgroup
     const int row = (warp % 4) * 32 + lane;  // TMEM lane = row within the Q tile
     const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;

@@ -152,7 +152,7 @@ int paired_items(int batch, int heads, int sq, int sk, int qtiles, int sms) {
 //   1: one 128-row Q tile per CTA, 2 K/V ring slots, MUFU exp2 only
 //   2: two 128-row Q tiles per CTA sharing each K/V tile (ping-pong),
 //      2 ring slots, 1/4 of exp2 on the FMA polynomial (Auto for sq >= 128)
-//   3: as 2 with 1/2 of exp2 on the polynomial
+//   3: as 2 with every exp2 on MUFU (no polynomial)
 // Varlen: a.sq / a.sk are the packed row counts, a.batch the number of
 // sequences, cu_q / cu_k their device offsets and max_sq the longest query
 // sequence (it sizes the tile grid).
@@ -230,14 +230,14 @@ int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream
     switch (config) {
       case 1: return launch_fwd<Causal, 1, 2, 0, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
       case 2: return launch_fwd<Causal, 2, 2, 2, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
-      case 3: return launch_fwd<Causal, 2, 2, 4, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
+      case 3: return launch_fwd<Causal, 2, 2, 0, true, false>(a, kv_heads, kv_begin, kv_end, splits, stream);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (config) {
     case 1: return launch_fwd<Causal, 1, 2, 0, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
     case 2: return launch_fwd<Causal, 2, 2, 2, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
-    case 3: return launch_fwd<Causal, 2, 2, 4, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
+    case 3: return launch_fwd<Causal, 2, 2, 0, false, false>(a, kv_heads, kv_begin, kv_end, 1, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -256,7 +256,7 @@ int dispatch_varlen(const Fav4Args& a, int config, int kv_heads, const int* cu_q
   switch (config) {
     case 1: return launch_fwd<Causal, 1, 2, 0, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
     case 2: return launch_fwd<Causal, 2, 2, 2, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
-    case 3: return launch_fwd<Causal, 2, 2, 4, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
+    case 3: return launch_fwd<Causal, 2, 2, 0, false, true>(a, kv_heads, 0, a.sk, 1, stream, cu_q, cu_k, max_sq);
     default: return cudaErrorInvalidValue;
   }
 }
