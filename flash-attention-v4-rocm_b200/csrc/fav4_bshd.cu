@@ -248,6 +248,22 @@ int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream
 extern "C" int fav4_bshd_select_config(const Fav4Args* a) { return a->sq < 128 ? 1 : 2; }
 
 namespace fav4 {
+// Auto for one full launch (fav4_bshd_forward, _gqa, _host): the reference's
+// rule, then one-Q-tile work tiles when two-tile ones would occupy at most half
+// of the SMs. With so few tiles the SMs would idle anyway, and twice as many
+// 128-row tiles spread the work wider (measured +8-15 % at B4 S512 and B8 S256,
+// while at 0.86 of the SMs (B4 S1024) two-tile tiles are still faster dense).
+int auto_config(const Fav4Args* a) {
+  const int c = fav4_bshd_select_config(a);
+  int dev = 0;
+  DeviceInfo info;
+  if (c != 2 || cudaGetDevice(&dev) != cudaSuccess || !device_info(dev, &info)) return c;
+  const int64_t tiles = static_cast<int64_t>(a->batch) * a->heads * ((a->sq + 2 * kBlockM - 1) / (2 * kBlockM));
+  return 2 * tiles <= info.sms ? 1 : c;
+}
+}  // namespace fav4
+
+namespace fav4 {
 namespace {
 
 template <bool Causal>
@@ -291,7 +307,7 @@ extern "C" int fav4_bshd_forward_varlen(const Fav4VarlenArgs* v, int causal, int
 
 extern "C" int fav4_bshd_forward(const Fav4Args* a, int causal, int config, cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config)) return cudaErrorInvalidValue;
-  if (config == 0) config = fav4_bshd_select_config(a);
+  if (config == 0) config = fav4::auto_config(a);
   return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream)
                 : fav4::dispatch<false>(*a, config, 0, a->sk, stream);
 }
@@ -300,7 +316,7 @@ extern "C" int fav4_bshd_forward_gqa(const Fav4Args* a, int kv_heads, int causal
                                      cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || kv_heads < 1 || kv_heads > a->heads || a->heads % kv_heads)
     return cudaErrorInvalidValue;
-  if (config == 0) config = fav4_bshd_select_config(a);
+  if (config == 0) config = fav4::auto_config(a);
   return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream, kv_heads)
                 : fav4::dispatch<false>(*a, config, 0, a->sk, stream, kv_heads);
 }
@@ -515,7 +531,9 @@ extern "C" int fav4_bshd_forward_host(const Fav4Args* a, const Fav4HostOut* outs
       out += l.o;
       ca.lse = dst_lse[j] = outs[j].lse ? reinterpret_cast<float*>(out) : nullptr;
       if (outs[j].lse) out += l.lse;
-      e = static_cast<cudaError_t>(fav4_bshd_forward(&ca, outs[j].causal, outs[j].config, stream));
+      // Auto is resolved on the whole batch, so chunking never changes the numbers.
+      e = static_cast<cudaError_t>(
+          fav4_bshd_forward(&ca, outs[j].causal, outs[j].config ? outs[j].config : fav4::auto_config(a), stream));
     }
     if (e == cudaSuccess) e = cudaEventRecord(pipe.computed[s], stream);
     // download

@@ -32,7 +32,9 @@ typedef struct Fav4Args Fav4Args;
  * c <= r), equal Q/K/V heads, positive finite scale, finite dot products.
  * The stream belongs to the calling device; the call allocates nothing and
  * never synchronises the host, so it can be captured in a CUDA graph.
- * config 0 = Auto (fav4_bshd_select_config), 1/2/3 = explicit tilings.
+ * config 0 = Auto: fav4_bshd_select_config's rule, except that config 1 is
+ * taken when config 2's work tiles (batch * heads * ceil(sq / 256)) would
+ * occupy at most half of the device's SMs; 1/2/3 = explicit tilings.
  * Returns 0 on success, cudaErrorInvalidValue (1) on invalid arguments or
  * config, else the launch status (cudaGetLastError).
  *
@@ -40,7 +42,9 @@ typedef struct Fav4Args Fav4Args;
  * src/bshd.hip:26-38. */
 int fav4_bshd_forward(const Fav4Args* args, int causal, int config, cudaStream_t stream);
 
-/* Auto configuration: 1 when sq < 128, else 2.
+/* The reference's auto configuration: 1 when sq < 128, else 2 (the Auto of
+ * fav4_bshd_forward adds the few-tiles rule above; the partial, split-KV and
+ * packed-sequence entries use this rule as it is).
  * Replaces: fav4_bshd_select_config, reference include/fav4_bshd.h:20 and
  * src/bshd.hip:23-25. */
 int fav4_bshd_select_config(const Fav4Args* args);

@@ -46,9 +46,11 @@ def test_opcheck():
 def test_inside_torch_compile_graph():
     q, k, v = _inputs(2, 4, 256, 256, seed=6)
 
+    # elementwise work around the operator only: a reduction's order may
+    # differ between Inductor and eager, which says nothing about the operator
     def block(q, k, v):
         o = ops.attention(q * 0.5, k, v, causal=True)
-        return o.float().sum(dim=-1)
+        return o.float() * 2.0 + 1.0
 
     want = block(q, k, v)
     got = torch.compile(block, fullgraph=True)(q, k, v)
