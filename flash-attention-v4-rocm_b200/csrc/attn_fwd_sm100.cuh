@@ -389,6 +389,9 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // Split launches are followed by the combine as a programmatic dependent
+  // launch: let it be scheduled now (it waits for this grid's writes itself).
+  if (Split) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int list_len = Paired ? tile_list[kMaxListTiles] : 0;  // paired schedule: this CTA's tiles
 
   // 384 threads launched with kLaunchRegs registers each (ptxas must report

@@ -24,6 +24,9 @@ struct CombineParams {
 };
 
 __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ CombineParams p) {
+  // Launched as a programmatic dependent of the split kernel: wait until its
+  // partials are written (returns at once for an ordinary launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x % 32;
   const int64_t total = static_cast<int64_t>(p.batch) * p.sq * p.heads;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);

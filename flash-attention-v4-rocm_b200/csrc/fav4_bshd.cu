@@ -335,8 +335,12 @@ namespace fav4 {
 namespace {
 
 // The combine launch for 1..kCombineCapacity parts (arguments validated as fav4_bshd_combine does).
+// after_split: the launch directly follows the one-launch split kernel on the
+// same stream, so it goes out as a programmatic dependent launch: it is
+// scheduled while the split kernel's last CTAs run and waits in
+// griddepcontrol.wait until that kernel's writes are visible.
 int combine_parts(const void* const* o_parts, const float* const* lse_parts, int parts, void* o, float* lse,
-                  int batch, int heads, int sq, cudaStream_t stream) {
+                  int batch, int heads, int sq, cudaStream_t stream, bool after_split = false) {
   if (!o_parts || !lse_parts || !o || parts < 1 || parts > kCombineCapacity || batch <= 0 || heads <= 0 ||
       sq <= 0 || batch > INT_MAX / heads || heads > INT_MAX / 128 || sq > INT_MAX / (heads * 128) ||
       (reinterpret_cast<uintptr_t>(o) & 15) || (reinterpret_cast<uintptr_t>(lse) & 3))
@@ -364,8 +368,20 @@ int combine_parts(const void* const* o_parts, const float* const* lse_parts, int
   const int64_t want = (rows + 7) / 8;  // 8 warps per block, one row per warp per pass
   const int64_t cap = static_cast<int64_t>(info.sms) * 8;
   const int grid = static_cast<int>(want < cap ? want : cap);
-  combine_kernel<<<grid, 256, 0, stream>>>(p);
-  return cudaGetLastError();
+  if (!after_split) {
+    combine_kernel<<<grid, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_kernel, p);
 }
 
 }  // namespace
@@ -638,7 +654,7 @@ int splitkv_range(const Fav4Args* a, int causal, int config, int kv_begin, int k
   const int e = causal ? dispatch<true>(pa, config, kv_begin, kv_end, stream, 0, splits)
                        : dispatch<false>(pa, config, kv_begin, kv_end, stream, 0, splits);
   if (e != cudaSuccess) return e;
-  return combine_parts(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream);
+  return combine_parts(o_parts, lse_parts, splits, a->o, a->lse, a->batch, a->heads, a->sq, stream, true);
 }
 
 }  // namespace
