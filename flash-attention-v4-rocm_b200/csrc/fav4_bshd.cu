@@ -248,11 +248,14 @@ int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream
 extern "C" int fav4_bshd_select_config(const Fav4Args* a) { return a->sq < 128 ? 1 : 2; }
 
 namespace fav4 {
-// Auto for one full launch (fav4_bshd_forward, _gqa, _host): the reference's
-// rule, then one-Q-tile work tiles when two-tile ones would occupy at most half
-// of the SMs. With so few tiles the SMs would idle anyway, and twice as many
-// 128-row tiles spread the work wider (measured +8-15 % at B4 S512 and B8 S256,
-// while at 0.86 of the SMs (B4 S1024) two-tile tiles are still faster dense).
+// Auto of the whole-key-range entries (fav4_bshd_forward, _gqa, _host and the
+// one-launch split-KV ones): the reference's rule, then one-Q-tile work tiles
+// when two-tile ones (without key splits) would occupy at most half of the SMs.
+// With so few tiles the SMs would idle anyway, and twice as many 128-row tiles
+// spread the work wider (measured +8-15 % at B4 S512 and B8 S256, while at 0.86
+// of the SMs (B4 S1024) two-tile tiles are still faster dense); decode shapes
+// with Sq = 128 get the double-buffered one-tile kernel instead of a two-tile
+// one whose second tile is empty.
 int auto_config(const Fav4Args* a) {
   const int c = fav4_bshd_select_config(a);
   int dev = 0;
@@ -601,7 +604,7 @@ int64_t base_tiles(const Fav4Args* a, int config) {
 
 extern "C" int fav4_bshd_splitkv_splits(const Fav4Args* a, int causal, int config) {
   if (!fav4::args_valid(a, causal, config)) return -1;
-  if (config == 0) config = fav4_bshd_select_config(a);
+  if (config == 0) config = fav4::auto_config(a);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   fav4::DeviceInfo info;
@@ -664,7 +667,7 @@ extern "C" int fav4_bshd_forward_splitkv(const Fav4Args* a, int causal, int conf
                                          size_t workspace_bytes, cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || splits < 0 || splits > fav4::kCombineCapacity)
     return cudaErrorInvalidValue;
-  if (config == 0) config = fav4_bshd_select_config(a);
+  if (config == 0) config = fav4::auto_config(a);
   if (splits == 0) splits = fav4_bshd_splitkv_splits(a, causal, config);
   if (splits < 1) return cudaErrorInvalidValue;
   if (splits == 1) return fav4_bshd_forward(a, causal, config, stream);
@@ -718,7 +721,7 @@ extern "C" int fav4_bshd_forward_splitkv_static(const Fav4Args* a, int causal, i
                                                 cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || splits < 1 || splits > fav4::kMaxCombineParts)
     return cudaErrorInvalidValue;
-  if (config == 0) config = fav4_bshd_select_config(a);
+  if (config == 0) config = fav4::auto_config(a);
   if (splits == 1) return fav4_bshd_forward(a, causal, config, stream);  // one slice: no partials
   const size_t need = fav4_bshd_splitkv_workspace_bytes(a, splits);
   if (need == 0 || need > fav4::kStaticScratchBytes) return cudaErrorMemoryAllocation;

@@ -43,8 +43,9 @@ typedef struct Fav4Args Fav4Args;
 int fav4_bshd_forward(const Fav4Args* args, int causal, int config, cudaStream_t stream);
 
 /* The reference's auto configuration: 1 when sq < 128, else 2 (the Auto of
- * fav4_bshd_forward adds the few-tiles rule above; the partial, split-KV and
- * packed-sequence entries use this rule as it is).
+ * fav4_bshd_forward, _gqa, _host and the one-launch split-KV entries adds the
+ * few-tiles rule above; the partial and packed-sequence entries use this rule
+ * as it is).
  * Replaces: fav4_bshd_select_config, reference include/fav4_bshd.h:20 and
  * src/bshd.hip:23-25. */
 int fav4_bshd_select_config(const Fav4Args* args);
