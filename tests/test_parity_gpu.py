@@ -230,5 +230,23 @@ def test_partial_rows_without_keys_are_empty(runner, cuda):
     check(o, lse, ref, ref_lse, np.arange(150, 400))
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_auto_takes_one_tile_kernel_for_few_tiles(runner, cuda, causal):
+    """Auto (config 0) is the reference's rule (sq < 128 -> 1, else 2) except
+    that config 1 runs when config 2's work tiles, B*H*ceil(Sq/256), would
+    fill at most half of the SMs; the two configs round exp2 differently, so
+    bit identity shows which kernel ran."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    for b, h, s in ((1, 4, 512), (max(1, sms // 16), 8, 512), (sms, 8, 256)):
+        q, k, v = (torch.randn(b, s, h, 128, generator=gen, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+        auto, one, two = (run(runner, q, k, v, causal, c) for c in (0, 1, 2))
+        want = one if 2 * b * h * ((s + 255) // 256) <= sms else two
+        assert torch.equal(auto[0], want[0]) and torch.equal(auto[1], want[1]), (b, h, s)
+        ref, ref_lse = R.reference_chunked(*(x.float().cpu().numpy() for x in (q, k, v)), causal,
+                                           np.arange(0, s, 37))
+        check(auto[0], auto[1], ref, ref_lse, np.arange(0, s, 37))
+
+
 def test_no_pipeline_timeouts_recorded(runner, cuda):
     assert runner.pipeline_status(clear=False) == 0
