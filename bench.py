@@ -80,6 +80,22 @@ def flops(b, h, s, causal):
 STEP_FLOPS = flops(B, H, S, False) + flops(B, H, S, True)
 
 
+def dense_kernel_label(nb, config):
+    """The forward kernel a dense launch of B=nb, H, S runs: the library's Auto
+    rule (include/fav4_bshd.h, config 0), restated here only to name it."""
+    if config != 0:
+        return f"attn_fwd_sm100_kernel (dense, config {config})"
+    if S < 128:
+        return "attn_fwd_sm100_kernel (dense, config Auto=1)"
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    t2, tw = nb * H * (-(-S // 256)), nb * H * (-(-S // 128))
+    if 2 * t2 <= sms:
+        return "attn_fwd_sm100_kernel (dense, config Auto=1)"
+    if S >= 2048 and (-(-tw // sms)) * 25 < (-(-t2 // sms)) * 46:
+        return "attn_fwd_wide_kernel (dense, Auto: wide-step kernel)"
+    return "attn_fwd_sm100_kernel (dense, config Auto=2)"
+
+
 def peaks():
     try:
         return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
@@ -1051,7 +1067,7 @@ def run_bench(args, rank, world, local):
     long_region = region_max > 2000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
     traffic = committed_traffic()
-    roofline = {"bound": "tensor", "kernel": f"attn_fwd_sm100_kernel (dense, config Auto=2), B{nb} per GPU",
+    roofline = {"bound": "tensor", "kernel": f"{dense_kernel_label(nb, args.config)}, B{nb} per GPU",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16",
                 "traffic": (traffic.get("dense_dram_bytes_per_launch") if traffic and nb == 32 else None),

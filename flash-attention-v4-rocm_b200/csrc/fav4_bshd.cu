@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "attn_fwd_sm100.cuh"
+#include "attn_fwd_wide_sm100.cuh"
 #include "attn_bwd_sm100.cuh"
 #include "attn_bwd_fused_sm100.cuh"
 #include "combine.cuh"
@@ -222,6 +223,58 @@ int launch_fwd(const Fav4Args& a, int kv_heads, int kv_begin, int kv_end, int sp
   return cudaGetLastError();
 }
 
+// Wide-step kernel (attn_fwd_wide_sm100.cuh): one 128-row Q tile per CTA,
+// 256 keys per step; whole key range, no splits, no packed sequences; dense
+// only (Auto never picks it for causal launches).
+template <bool Causal>
+int launch_fwd_wide(const Fav4Args& a, int kv_heads, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  DeviceInfo info;
+  if (!device_info(dev, &info)) return cudaErrorInvalidDevice;
+  constexpr int smem = WideLayout::kAlloc;
+  auto kernel = attn_fwd_wide_kernel<Causal, 2>;  // 2 of 8 exp2 columns on the polynomial, as config 2
+  {
+    static std::mutex mu;
+    static bool attr_set[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  CUtensorMap tq, tk, tv;
+  if (!encode_bshd(&tq, a.q, a.batch, a.sq, a.heads) || !encode_bshd(&tk, a.k, a.batch, a.sk, kv_heads, kWideN) ||
+      !encode_bshd(&tv, a.v, a.batch, a.sk, kv_heads, kWideN))
+    return cudaErrorInvalidValue;
+  FwdParams p = {};
+  p.o = static_cast<__nv_bfloat16*>(a.o);
+  p.lse = a.lse;
+  p.batch = a.batch;
+  p.heads = a.heads;
+  p.sq = a.sq;
+  p.sk = a.sk;
+  p.kv_group = a.heads / kv_heads;
+  p.kv_begin = 0;
+  p.kv_end = a.sk;
+  p.splits = 1;
+  p.kv_chunk = a.sk;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.num_mblocks = (a.sq + kBlockM - 1) / kBlockM;
+  const int64_t tiles = static_cast<int64_t>(a.batch) * a.heads * p.num_mblocks;
+  if (tiles > INT_MAX) return cudaErrorInvalidValue;
+  p.num_base_tiles = static_cast<int>(tiles);
+  p.num_tiles = static_cast<int>(tiles);
+  p.num_items = 0;
+  p.status = info.status;
+  p.wait_limit_ns = wait_limit_ns();
+  const int grid = static_cast<int>(tiles < info.sms ? tiles : info.sms);
+  kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError();
+}
+
 template <bool Causal>
 int dispatch(const Fav4Args& a, int config, int kv_begin, int kv_end, cudaStream_t stream, int kv_heads = 0,
              int splits = 1) {
@@ -256,13 +309,28 @@ namespace fav4 {
 // of the SMs (B4 S1024) two-tile tiles are still faster dense); decode shapes
 // with Sq = 128 get the double-buffered one-tile kernel instead of a two-tile
 // one whose second tile is empty.
-int auto_config(const Fav4Args* a) {
+//
+// Dense launches of the full key range (allow_wide: fav4_bshd_forward, _gqa,
+// _host) then take the wide-step kernel (kConfigWide) when its 128-row tiles
+// fill the last wave so much better that its 0.92x per-tile speed (B32 S4096)
+// still wins: waves(128-row tiles) < 1.84 x waves(256-row tiles), with Sk >=
+// 2048 (shorter key ranges favour the two-tile kernel). Measured: B4 S4096
+// 1.05x, B2 S8192 1.08x, B1 S16384 1.08x, B5 S4096 1.02x; B3 S4096 and B4
+// S3072, where the rule keeps config 2, would lose 3-5 %.
+constexpr int kConfigWide = 4;  // internal: never accepted from callers
+int auto_config(const Fav4Args* a, bool causal = true, bool allow_wide = false) {
   const int c = fav4_bshd_select_config(a);
   int dev = 0;
   DeviceInfo info;
   if (c != 2 || cudaGetDevice(&dev) != cudaSuccess || !device_info(dev, &info)) return c;
   const int64_t tiles = static_cast<int64_t>(a->batch) * a->heads * ((a->sq + 2 * kBlockM - 1) / (2 * kBlockM));
-  return 2 * tiles <= info.sms ? 1 : c;
+  if (2 * tiles <= info.sms) return 1;
+  if (allow_wide && !causal && a->sk >= 2048) {
+    const int64_t tiles_w = static_cast<int64_t>(a->batch) * a->heads * ((a->sq + kBlockM - 1) / kBlockM);
+    const int64_t waves = (tiles + info.sms - 1) / info.sms, waves_w = (tiles_w + info.sms - 1) / info.sms;
+    if (waves_w * 25 < waves * 46) return kConfigWide;
+  }
+  return c;
 }
 }  // namespace fav4
 
@@ -310,16 +378,23 @@ extern "C" int fav4_bshd_forward_varlen(const Fav4VarlenArgs* v, int causal, int
 
 extern "C" int fav4_bshd_forward(const Fav4Args* a, int causal, int config, cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config)) return cudaErrorInvalidValue;
-  if (config == 0) config = fav4::auto_config(a);
+  if (config == 0) config = fav4::auto_config(a, causal != 0, true);
+  if (config == fav4::kConfigWide) return fav4::launch_fwd_wide<false>(*a, a->heads, stream);
   return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream)
                 : fav4::dispatch<false>(*a, config, 0, a->sk, stream);
+}
+
+extern "C" int fav4_bshd_forward_wide(const Fav4Args* a, cudaStream_t stream) {
+  if (!fav4::args_valid(a, 0, 0)) return cudaErrorInvalidValue;
+  return fav4::launch_fwd_wide<false>(*a, a->heads, stream);
 }
 
 extern "C" int fav4_bshd_forward_gqa(const Fav4Args* a, int kv_heads, int causal, int config,
                                      cudaStream_t stream) {
   if (!fav4::args_valid(a, causal, config) || kv_heads < 1 || kv_heads > a->heads || a->heads % kv_heads)
     return cudaErrorInvalidValue;
-  if (config == 0) config = fav4::auto_config(a);
+  if (config == 0) config = fav4::auto_config(a, causal != 0, true);
+  if (config == fav4::kConfigWide) return fav4::launch_fwd_wide<false>(*a, kv_heads, stream);
   return causal ? fav4::dispatch<true>(*a, config, 0, a->sk, stream, kv_heads)
                 : fav4::dispatch<false>(*a, config, 0, a->sk, stream, kv_heads);
 }
@@ -551,8 +626,9 @@ extern "C" int fav4_bshd_forward_host(const Fav4Args* a, const Fav4HostOut* outs
       ca.lse = dst_lse[j] = outs[j].lse ? reinterpret_cast<float*>(out) : nullptr;
       if (outs[j].lse) out += l.lse;
       // Auto is resolved on the whole batch, so chunking never changes the numbers.
-      e = static_cast<cudaError_t>(
-          fav4_bshd_forward(&ca, outs[j].causal, outs[j].config ? outs[j].config : fav4::auto_config(a), stream));
+      const int cfg = outs[j].config ? outs[j].config : fav4::auto_config(a, outs[j].causal != 0, true);
+      e = static_cast<cudaError_t>(cfg == fav4::kConfigWide ? fav4::launch_fwd_wide<false>(ca, ca.heads, stream)
+                                                             : fav4_bshd_forward(&ca, outs[j].causal, cfg, stream));
     }
     if (e == cudaSuccess) e = cudaEventRecord(pipe.computed[s], stream);
     // download

@@ -24,14 +24,15 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // BSHD bf16 tensor [B, S, H, 128] as a 4-D TMA map {128, H, S, B} with a
-// {64, 1, 128, 1} box and 128-byte swizzle; rows past S read as zero.
-inline bool encode_bshd(CUtensorMap* map, const void* base, int b, int s, int h) {
+// {64, 1, box_rows, 1} box (box_rows <= 256) and 128-byte swizzle; rows past S
+// read as zero.
+inline bool encode_bshd(CUtensorMap* map, const void* base, int b, int s, int h, int box_rows = 128) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(s),
                               static_cast<cuuint64_t>(b)};
   const cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(h) * 256, static_cast<cuuint64_t>(s) * h * 256};
-  const cuuint32_t box[4] = {64, 1, 128, 1};
+  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
   const cuuint32_t elem[4] = {1, 1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, elem,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -64,6 +64,8 @@ _PROBE = None
 def _bind(lib):
     lib.fav4_bshd_forward.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_void_p]
     lib.fav4_bshd_forward.restype = C.c_int
+    lib.fav4_bshd_forward_wide.argtypes = [C.POINTER(Args), C.c_void_p]
+    lib.fav4_bshd_forward_wide.restype = C.c_int
     lib.fav4_bshd_select_config.argtypes = [C.POINTER(Args)]
     lib.fav4_bshd_select_config.restype = C.c_int
     lib.fav4_bshd_forward_splitkv.argtypes = [C.POINTER(Args), C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
@@ -181,6 +183,13 @@ class Runner:
         status = self.lib.fav4_bshd_forward(C.byref(a), int(causal), config, _stream(stream))
         if status:
             raise RuntimeError(f"config {config}: CUDA status {status}")
+
+    def call_wide(self, q, k, v, o, lse, scale=None, stream=None):
+        """Dense forward through the wide-step kernel (fav4_bshd_forward_wide)."""
+        a = self.args(q, k, v, o, lse, scale)
+        status = self.lib.fav4_bshd_forward_wide(C.byref(a), _stream(stream))
+        if status:
+            raise RuntimeError(f"wide: CUDA status {status}")
 
     def call_splitkv(self, q, k, v, o, lse, causal, config=0, splits=0, scale=None, stream=None, workspace=None):
         """Split-KV forward in one launch (fav4_bshd_forward_splitkv), for few

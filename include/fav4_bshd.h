@@ -34,7 +34,10 @@ typedef struct Fav4Args Fav4Args;
  * never synchronises the host, so it can be captured in a CUDA graph.
  * config 0 = Auto: fav4_bshd_select_config's rule, except that config 1 is
  * taken when config 2's work tiles (batch * heads * ceil(sq / 256)) would
- * occupy at most half of the device's SMs; 1/2/3 = explicit tilings.
+ * occupy at most half of the device's SMs, and that dense launches with
+ * sk >= 2048 take the wide-step kernel (fav4_bshd_forward_wide) when its
+ * 128-row tiles need fewer than 1.84x the waves of config 2's 256-row tiles;
+ * 1/2/3 = explicit tilings.
  * Returns 0 on success, cudaErrorInvalidValue (1) on invalid arguments or
  * config, else the launch status (cudaGetLastError).
  *
@@ -49,6 +52,16 @@ int fav4_bshd_forward(const Fav4Args* args, int causal, int config, cudaStream_t
  * Replaces: fav4_bshd_select_config, reference include/fav4_bshd.h:20 and
  * src/bshd.hip:23-25. */
 int fav4_bshd_select_config(const Fav4Args* args);
+
+/* Dense forward through the wide-step kernel whatever the shape: one 128-row
+ * Q tile per CTA against 256 keys per step (S as a 128x256 MMA, P in TMEM
+ * columns of its own, the 256 keys' softmax split over two warpgroups).
+ * fav4_bshd_forward's Auto takes it for dense launches whose 256-row tiles
+ * would leave the last wave poorly filled (see config 0 above); this entry
+ * runs it on any valid dense problem. Same arguments, checks and return codes
+ * as fav4_bshd_forward with causal = 0 and config = 0 (no reference
+ * counterpart: the reference has one kernel per config, src/bshd.hip:26-38). */
+int fav4_bshd_forward_wide(const Fav4Args* args, cudaStream_t stream);
 
 /* Grouped-query attention (no reference counterpart: the reference requires
  * equal Q/K/V heads, include/fav4_bshd.h:15). args->heads is the number of
