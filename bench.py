@@ -87,6 +87,7 @@ def dense_kernel_label(nb, config):
         return f"attn_fwd_sm100_kernel (dense, config {config})"
     if S < 128:
         return "attn_fwd_sm100_kernel (dense, config Auto=1)"
+    import torch
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     t2, tw = nb * H * (-(-S // 256)), nb * H * (-(-S // 128))
     if 2 * t2 <= sms:
