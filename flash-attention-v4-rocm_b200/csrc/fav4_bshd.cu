@@ -446,8 +446,18 @@ int combine_parts(const void* const* o_parts, const float* const* lse_parts, int
   const int64_t want = (rows + 7) / 8;  // 8 warps per block, one row per warp per pass
   const int64_t cap = static_cast<int64_t>(info.sms) * 8;
   const int grid = static_cast<int>(want < cap ? want : cap);
+  // the smallest compile-time part bound that fits, 32-bit row indices when they suffice
+  void (*kernel)(CombineParams);
+  const bool idx64 = rows > static_cast<int64_t>(INT32_MAX);
+  if (parts <= 2) kernel = idx64 ? combine_kernel<2, true> : combine_kernel<2, false>;
+  else if (parts <= 4) kernel = idx64 ? combine_kernel<4, true> : combine_kernel<4, false>;
+  else if (parts <= 8) kernel = idx64 ? combine_kernel<8, true> : combine_kernel<8, false>;
+  else if (parts <= 16) kernel = idx64 ? combine_kernel<16, true> : combine_kernel<16, false>;
+  else kernel = idx64 ? combine_kernel<32, true> : combine_kernel<32, false>;
+  if (parts > 8 && rows <= static_cast<int64_t>(grid) * 8)  // one row per warp: all loads at once
+    kernel = parts <= 16 ? combine_kernel<16, false, true> : combine_kernel<32, false, true>;
   if (!after_split) {
-    combine_kernel<<<grid, 256, 0, stream>>>(p);
+    kernel<<<grid, 256, 0, stream>>>(p);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -459,7 +469,7 @@ int combine_parts(const void* const* o_parts, const float* const* lse_parts, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, combine_kernel, p);
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 }  // namespace
