@@ -17,7 +17,8 @@ def _host(shape, gen, dtype=torch.bfloat16):
 
 
 @pytest.mark.parametrize("b,h,sq,sk,chunks", [(5, 4, 300, 517, 3), (5, 4, 300, 517, 1), (3, 2, 128, 128, 8),
-                                              (4, 8, 1000, 1000, 4), (1, 3, 77, 2049, 2)])
+                                              (4, 8, 1000, 1000, 4), (1, 3, 77, 2049, 2),
+                                              (4, 8, 4096, 4096, 4)])  # dense Auto: the wide-step kernel
 def test_host_forward_matches_device_forward(runner, b, h, sq, sk, chunks):
     gen = torch.Generator().manual_seed(b * 1000 + sq + chunks)
     q, k, v = _host((b, sq, h, 128), gen), _host((b, sk, h, 128), gen), _host((b, sk, h, 128), gen)
